@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 radix sort (one JSON line on rank 0).
+
+Default workload (N=1): BASELINE config 2 -- SortPairs ascending of 2^26
+int32 keys uniform over all 32 bits with uint32 values = original index,
+through the library's in/out-pointer C ABI (cusort_sort_pairs).  A "step" is
+one complete sort call (init + histogram + 4 onesweep passes).
+
+  value     Gkeys/s with inputs resident in HBM (inputs are 512 MiB > L2,
+            so no L2 flush is needed between steps)
+  e2e       same metric through the same C ABI with HOST buffers: pinned
+            H2D copy of keys+values, sort, D2H copy of sorted keys+values
+  roofline  onesweep kernel: algorithmic bytes 2*n*(K+V) per launch over its
+            CUDA-event launch duration (measured live in a second pass with
+            per-kernel events), against MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the oracle's parallel std::stable_sort on the host cores,
+            bounded sample
+
+--impl reference times the UNMODIFIED reference library compiled for sm_100a
+(oracle/_ref) on the same workload through its own public API.
+
+N>1 (torchrun): sharded multi-GPU sort, 2^26 pairs per GPU (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Gkeys/s (2^26 int32 keys + uint32 values, SortPairs, 1 GPU)"
+UNIT = "Gkeys/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--log2n", type=int, default=26)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs"], default=None,
+                    help="only run --warmup + --steps sorts of this case (for ncu captures)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi) around the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, t0: float, t1: float):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ts, line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            rows.append((ts, parts))
+        inside = [r for r in rows if t0 <= r[0] <= t1] or rows
+        sm = [float(p[1]) for _, p in inside if p[1].replace(".", "").isdigit()]
+        mx = [float(p[2]) for _, p in inside if p[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for _, p in inside:
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(inside),
+                "window": "timed region" if any(t0 <= r[0] <= t1 for r in rows) else "whole run"}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def make_inputs(torch, n: int, seed: int, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    keys = torch.randint(-(2 ** 31), 2 ** 31, (n,), dtype=torch.int64, device=device, generator=g).to(torch.int32)
+    vals = torch.arange(n, dtype=torch.int32, device=device)  # uint32 bit pattern = index
+    return keys, vals
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+def traffic_from_profiles(workload: str):
+    p = ROOT / "profiles" / "onesweep_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(workload)
+
+
+class Sorter:
+    """One SortPairs/SortKeys call through a C ABI (ours or the reference's)."""
+
+    def __init__(self, impl, torch, kt_name, kid, kb, vb, n, keys_in, keys_out, vals_in, vals_out, stream):
+        self.torch = torch
+        self.impl = impl
+        self.n = n
+        s = C.c_void_p(stream)
+        kin, kout = C.c_void_p(keys_in.data_ptr()), C.c_void_p(keys_out.data_ptr())
+        vin = C.c_void_p(vals_in.data_ptr()) if vb else None
+        vout = C.c_void_p(vals_out.data_ptr()) if vb else None
+        if impl == "ours":
+            from libcusort_b200 import _capi
+            lib = _capi.load()
+            if vb:
+                self.call = lambda t, tb: lib.cusort_sort_pairs(t, C.byref(tb), kid, kin, kout, vb, vin, vout, n, 0,
+                                                               8 * kb, s)
+            else:
+                self.call = lambda t, tb: lib.cusort_sort_keys(t, C.byref(tb), kid, kin, kout, n, 0, 8 * kb, s)
+            self.lib = lib
+        else:
+            from oracle import oracle as O
+            rl = O._load_ref()
+            fn = getattr(rl, f"ref_sort_k{kid}")
+            ks, vs = C.c_int(0), C.c_int(0)
+            self.call = lambda t, tb: fn(vb, 0, 1, t, C.byref(tb), kin, kout, C.byref(ks), vin, vout, C.byref(vs),
+                                         n, 0, 8 * kb, s)
+        tb = C.c_size_t(0)
+        rc = self.call(None, tb)
+        if rc != 0:
+            raise RuntimeError(f"size query failed rc={rc}")
+        self.temp = torch.empty(max(tb.value, 1), dtype=torch.uint8, device=keys_in.device)
+        self.tp = C.c_void_p(self.temp.data_ptr())
+        self.tb = C.c_size_t(tb.value)
+
+    def __call__(self):
+        rc = self.call(self.tp, self.tb)
+        if rc != 0:
+            raise RuntimeError(f"sort failed rc={rc}")
+
+
+def time_steps(torch, fn, steps: int, warmup: int, dist=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    return a.elapsed_time(b)
+
+
+def e2e_measure(torch, sorter_factory, n, kb, vb, keys_host, vals_host, steps, warmup, device):
+    """Host buffers: per step H2D (keys, values), sort, D2H (sorted keys, values)."""
+    kin = torch.empty(n * kb, dtype=torch.uint8, device=device)
+    kout = torch.empty_like(kin)
+    vin = torch.empty(max(n * vb, 1), dtype=torch.uint8, device=device)
+    vout = torch.empty_like(vin)
+    ko_h = torch.empty(n * kb, dtype=torch.uint8, pin_memory=True)
+    vo_h = torch.empty(max(n * vb, 1), dtype=torch.uint8, pin_memory=True)
+    sorter = sorter_factory(kin, kout, vin, vout)
+
+    def step():
+        kin.copy_(keys_host, non_blocking=True)
+        if vb:
+            vin.copy_(vals_host, non_blocking=True)
+        sorter()
+        ko_h.copy_(kout, non_blocking=True)
+        if vb:
+            vo_h.copy_(vout, non_blocking=True)
+
+    ms = time_steps(torch, step, steps, warmup)
+    return ms / steps, ko_h, vo_h
+
+
+def cpu_baseline(seconds: float, n_full: int):
+    """Oracle parallel stable sort of int32/uint32 pairs on all host cores, bounded sample."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(2)
+    m = min(n_full, 1 << 22)
+    keys = rng.integers(-(2 ** 31), 2 ** 31, size=m, dtype=np.int64).astype(np.int32)
+    vals = np.arange(m, dtype=np.uint32)
+    reps, t_total = 0, 0.0
+    while t_total < seconds and reps < 1000:
+        t0 = time.perf_counter()
+        O.oracle_sort("i32", keys, vals, 0, 32, False, threads=cores)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    rate = reps * m / t_total / 1e9
+    return {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{reps} x {m} int32/uint32 pairs (2^{m.bit_length() - 1}), __gnu_parallel::stable_sort "
+                      f"over {cores} OpenMP threads, {t_total:.1f} s"}
+
+
+def run_single(args, torch, dist=None, rank=0, world=1):
+    device = torch.device("cuda", torch.cuda.current_device())
+    n = 1 << args.log2n
+    kt, kid, kb, vb = "i32", 5, 4, 4
+    keys, vals = make_inputs(torch, n, seed=2, device=device)
+    kin = keys.view(torch.uint8)
+    vin = vals.view(torch.uint8)
+    kout = torch.empty_like(kin)
+    vout = torch.empty_like(vin)
+    stream = torch.cuda.current_stream().cuda_stream
+    sorter = Sorter(args.impl, torch, kt, kid, kb, vb, n, kin, kout, vin, vout, stream)
+    smi = ClockSampler(device.index if device.index is not None else 0)
+    smi.start()
+    # extra untimed spin-up so clocks are settled and sampled
+    t_spin = time.time()
+    while time.time() - t_spin < 1.0:
+        sorter()
+        torch.cuda.synchronize()
+    t0 = time.time()
+    ms = time_steps(torch, sorter, args.steps, args.warmup, dist)
+    t1 = time.time()
+    clocks = smi.stop(t0 - 0.2, t1 + 0.2)
+    ms_step = ms / args.steps
+    value = n / (ms_step * 1e-3) / 1e9
+
+    # correctness spot check of the timed output (sortedness + permutation checksum)
+    ko = kout.view(torch.int32)
+    ok_sorted = bool((ko[1:] >= ko[:-1]).all().item())
+    vo = vout.view(torch.int32)
+    ok_stable = bool(torch.equal(keys[vo.long()], ko)) if ok_sorted else False
+
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int32 keys / uint32 values (integer radix)", "data": "synthetic (seeded uniform int32 keys, "
+        "values = index)",
+        "config": {"workload": "configs[1]: SortPairs 2^26 int32 keys uniform + uint32 index values", "n": n,
+                   "key": "int32", "value_bytes": 4, "api": "in/out pointers (cusort_sort_pairs)",
+                   "l2": "inputs 512 MiB > 126 MB L2 (no flush needed)"},
+        "verified": {"sorted": ok_sorted, "values_match_keys": ok_stable},
+        "clocks": clocks,
+    }
+    if args.impl == "ours":
+        P = 4
+        out["gpu_launches"] = args.steps * (2 + P)
+        # live per-kernel timing pass (events around each kernel, on the launch stream)
+        lib = sorter.lib
+        lib.cusort_set_kernel_timing(1)
+        acc = {0: [], 1: [], 2: []}
+        for _ in range(max(3, min(args.steps, 20))):
+            sorter()
+            buf = (C.c_float * 16)()
+            kinds = (C.c_int * 16)()
+            m = lib.cusort_get_kernel_times(buf, kinds, 16)
+            for i in range(m):
+                acc[kinds[i]].append(buf[i])
+        lib.cusort_set_kernel_timing(0)
+        os_ms = statistics.mean(acc[2])
+        h_ms = statistics.mean(acc[1])
+        peak, peak_src = peaks()
+        alg = 2 * n * (kb + vb)
+        achieved = alg / (os_ms * 1e-3) / 1e9
+        traffic = traffic_from_profiles("i32_u32_pairs_2^26")
+        out["roofline"] = {"bound": "hbm", "kernel": "onesweep_kernel", "achieved": achieved, "peak": peak,
+                           "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
+                           "traffic": traffic, "algorithmic_bytes_per_launch": alg,
+                           "launch_ms": os_ms, "histogram_launch_ms": h_ms,
+                           "histogram_gbs": n * kb / (h_ms * 1e-3) / 1e9,
+                           "whole_sort_frac": (4 * alg / (ms_step * 1e-3) / 1e9) / peak}
+    # e2e through the same C ABI with host buffers
+    keys_h = kin.cpu().pin_memory()
+    vals_h = vin.cpu().pin_memory()
+
+    def factory(a, b, c, d):
+        return Sorter(args.impl, torch, kt, kid, kb, vb, n, a, b, c, d, torch.cuda.current_stream().cuda_stream)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    e_ms, _, _ = e2e_measure(torch, factory, n, kb, vb, keys_h, vals_h, e2e_steps, 2, device)
+    out["e2e"] = {"value": n / (e_ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": n * (kb + vb),
+                  "d2h_bytes_per_step": n * (kb + vb), "ms_per_step": e_ms, "steps": e2e_steps,
+                  "path": "pinned host -> H2D -> sort (C ABI) -> D2H -> pinned host"}
+    if not args.no_secondary:
+        out["secondary"] = secondary(args, torch, device)
+    if args.impl == "ours" and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_seconds, n)
+    if args.impl == "reference":
+        out["impl"] = "reference"
+        out["cpu_baseline"] = {"value": value, "unit": UNIT, "cores": 0, "kind": "reference",
+                               "sample": "the reference library has no CPU path: this arm runs the UNMODIFIED "
+                                         "libcusort.cuh 1.0.1 built for sm_100a (nvcc 12.9, default build) on the "
+                                         "same B200, full workload"}
+    return out
+
+
+def secondary(args, torch, device):
+    """u32 keys-only 2^26 (the other single-GPU headline config), same impl."""
+    n = 1 << args.log2n
+    res = {}
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    kin = torch.randint(0, 256, (n * 4,), dtype=torch.uint8, device=device, generator=g)
+    kout = torch.empty_like(kin)
+    dummy = torch.empty(1, dtype=torch.uint8, device=device)
+    s = Sorter(args.impl, torch, "u32", 4, 4, 0, n, kin, kout, dummy, dummy, torch.cuda.current_stream().cuda_stream)
+    ms = time_steps(torch, s, max(10, args.steps), 3) / max(10, args.steps)
+    res["u32_keys_only_2^26"] = {"ms_per_step": ms, "gkeys_per_s": n / (ms * 1e-3) / 1e9,
+                                 "whole_sort_eff_gbs": 4 * 2 * n * 4 / (ms * 1e-3) / 1e9}
+    if args.impl == "ours":
+        lib = s.lib
+        lib.cusort_set_kernel_timing(1)
+        v = []
+        for _ in range(5):
+            s()
+            buf = (C.c_float * 16)()
+            kinds = (C.c_int * 16)()
+            m = lib.cusort_get_kernel_times(buf, kinds, 16)
+            v += [buf[i] for i in range(m) if kinds[i] == 2]
+        lib.cusort_set_kernel_timing(0)
+        res["u32_keys_only_2^26"]["onesweep_launch_ms"] = statistics.mean(v)
+        res["u32_keys_only_2^26"]["onesweep_gbs"] = 2 * n * 4 / (statistics.mean(v) * 1e-3) / 1e9
+    return res
+
+
+def profile_case(args, torch):
+    """Plain sorts of one case, nothing else (the command that ncu captures)."""
+    device = torch.device("cuda", 0)
+    n = 1 << args.log2n
+    if args.profile_case == "u32_keys":
+        kt, kid, kb, vb = "u32", 4, 4, 0
+    else:
+        kt, kid, kb, vb = "i32", 5, 4, 4
+    keys, vals = make_inputs(torch, n, seed=2, device=device)
+    kin, vin = keys.view(torch.uint8), vals.view(torch.uint8)
+    kout, vout = torch.empty_like(kin), torch.empty_like(vin)
+    s = Sorter(args.impl, torch, kt, kid, kb, vb, n, kin, kout, vin, vout, torch.cuda.current_stream().cuda_stream)
+    for _ in range(args.warmup + args.steps):
+        s()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "n": n, "impl": args.impl, "sorts": args.warmup + args.steps}))
+
+
+def main():
+    args = parse()
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 or args.gpus > 1:
+        from libcusort_b200 import mgpu_bench
+        out = mgpu_bench.run(args, torch)
+        if out is not None and rank == 0:
+            print(json.dumps(out))
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        sys.exit(1)
+    if args.impl == "reference":
+        from oracle import oracle as O
+        if not O.ref_available():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libcusort_ref.so was not built "
+                                                                  "(needs the reference checkout at build time)"}))
+            return
+    torch.cuda.set_device(0)
+    if args.profile_case:
+        profile_case(args, torch)
+        return
+    out = run_single(args, torch)
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/* cusort_b200.h -- C ABI of the B200-native LSD radix sort.
+ *
+ * Drop-in boundary for cusort::DeviceRadixSort (IlyaGrebnov/libcusort 1.0.1,
+ * libcusort.cuh).  The reference is a header-only C++ template library; the
+ * eight public overloads of DeviceRadixSort map one-to-one onto the eight
+ * sort entry points below, with the key type passed as a tag and the value
+ * type by its size (the reference itself maps values to uint8/16/32/64 or
+ * ulonglong2 by size, libcusort.cuh:2942-2953).  include/cusort_b200.cuh puts
+ * the reference's C++ templates (cusort::DoubleBuffer,
+ * cusort::DeviceRadixSort) back on top of these symbols.
+ *
+ * Semantics kept from the reference:
+ *   - d_temp_storage == NULL only writes *temp_storage_bytes and makes no
+ *     CUDA call (libcusort.cuh:2609-2613); trivial calls (num_items <= 1 or
+ *     begin_bit == end_bit) report 0 bytes, or 1 for the in/out-pointer form
+ *     with num_items > 0 (libcusort.cuh:2914-2919).
+ *   - DoubleBuffer form: both buffers are clobbered; afterwards each selector
+ *     is flipped once per 8-bit pass, i.e. selector ^= (passes & 1)
+ *     (libcusort.cuh:2685).
+ *   - In/out-pointer form: the result is in *_out, *_in is never written
+ *     (libcusort.cuh:2637-2641, 2668-2672); trivial calls copy in -> out.
+ *   - Stable; key order is the unsigned order of the twiddled key bits in
+ *     [begin_bit, end_bit) (signed: sign bit flipped; float/double: IEEE
+ *     total order, -0.0 < +0.0, NaN payloads kept; descending inverts the
+ *     bits, equal keys keep input order).
+ *   - cudaErrorInvalidValue when begin_bit < 0, end_bit < 0,
+ *     begin_bit > end_bit or end_bit > 8*sizeof(key) (libcusort.cuh:2908).
+ *   - Asynchronous on `stream`; no host synchronisation.
+ * Differences (stricter): an unknown key type, a value size outside
+ * {1,2,4,8,16}, a NULL temp_storage_bytes pointer, or a temp_storage_bytes
+ * below the size this library reported returns cudaErrorInvalidValue.
+ *
+ * All pointers are device pointers, naturally aligned for their element
+ * type.  The library allocates no device memory.
+ */
+#ifndef CUSORT_B200_H
+#define CUSORT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Key types of DeviceRadixSort (libcusort.cuh:2853: 1/2/4/8-byte arithmetic). */
+typedef enum cusort_key_type {
+  CUSORT_KEY_U8 = 0,
+  CUSORT_KEY_I8 = 1,
+  CUSORT_KEY_U16 = 2,
+  CUSORT_KEY_I16 = 3,
+  CUSORT_KEY_U32 = 4,
+  CUSORT_KEY_I32 = 5,
+  CUSORT_KEY_U64 = 6,
+  CUSORT_KEY_I64 = 7,
+  CUSORT_KEY_F32 = 8,
+  CUSORT_KEY_F64 = 9
+} cusort_key_type;
+
+/* Same layout as cusort::DoubleBuffer<T> (libcusort.cuh:156-184). */
+typedef struct cusort_double_buffer {
+  void* d_buffers[2];
+  int selector;
+} cusort_double_buffer;
+
+/* ---- DoubleBuffer overloads ------------------------------------------- */
+
+/* DeviceRadixSort::SortKeys(temp, bytes, DoubleBuffer<K>&, n, begin, end, stream)
+ * (libcusort.cuh:3004-3016). */
+cudaError_t cusort_sort_keys_db(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                                cusort_double_buffer* d_keys, int64_t num_items, int begin_bit, int end_bit,
+                                cudaStream_t stream);
+
+/* DeviceRadixSort::SortKeysDescending, DoubleBuffer (libcusort.cuh:3019-3031). */
+cudaError_t cusort_sort_keys_descending_db(void* d_temp_storage, size_t* temp_storage_bytes,
+                                           cusort_key_type key_type, cusort_double_buffer* d_keys,
+                                           int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
+
+/* DeviceRadixSort::SortPairs(temp, bytes, DoubleBuffer<K>&, DoubleBuffer<V>&, n, ...)
+ * (libcusort.cuh:2972-2984); value_bytes = sizeof(V). */
+cudaError_t cusort_sort_pairs_db(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                                 cusort_double_buffer* d_keys, size_t value_bytes, cusort_double_buffer* d_values,
+                                 int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
+
+/* DeviceRadixSort::SortPairsDescending, DoubleBuffer (libcusort.cuh:2988-3000). */
+cudaError_t cusort_sort_pairs_descending_db(void* d_temp_storage, size_t* temp_storage_bytes,
+                                            cusort_key_type key_type, cusort_double_buffer* d_keys,
+                                            size_t value_bytes, cusort_double_buffer* d_values,
+                                            int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
+
+/* ---- in/out-pointer overloads ------------------------------------------ */
+
+/* DeviceRadixSort::SortKeys(temp, bytes, const K* in, K* out, n, ...)
+ * (libcusort.cuh:3035-3048). */
+cudaError_t cusort_sort_keys(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                             const void* d_keys_in, void* d_keys_out, int64_t num_items, int begin_bit,
+                             int end_bit, cudaStream_t stream);
+
+/* DeviceRadixSort::SortKeysDescending, in/out (libcusort.cuh:3052-3065). */
+cudaError_t cusort_sort_keys_descending(void* d_temp_storage, size_t* temp_storage_bytes,
+                                        cusort_key_type key_type, const void* d_keys_in, void* d_keys_out,
+                                        int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
+
+/* DeviceRadixSort::SortPairs(temp, bytes, const K*, K*, const V*, V*, n, ...)
+ * (libcusort.cuh:3070-3085). */
+cudaError_t cusort_sort_pairs(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                              const void* d_keys_in, void* d_keys_out, size_t value_bytes,
+                              const void* d_values_in, void* d_values_out, int64_t num_items, int begin_bit,
+                              int end_bit, cudaStream_t stream);
+
+/* DeviceRadixSort::SortPairsDescending, in/out (libcusort.cuh:3089-3104). */
+cudaError_t cusort_sort_pairs_descending(void* d_temp_storage, size_t* temp_storage_bytes,
+                                         cusort_key_type key_type, const void* d_keys_in, void* d_keys_out,
+                                         size_t value_bytes, const void* d_values_in, void* d_values_out,
+                                         int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
+
+/* ---- library state, status and diagnostics (no reference counterpart;
+ *      the reference has compile-time macros only, libcusort.cuh:119-148) -- */
+
+/* "1.0.1-b200.N": reference API version this build is a drop-in for. */
+const char* cusort_version(void);
+
+/* Launch modes: 0 = one launch per kernel with programmatic dependent launch
+ * (default), 1 = CUDA graph per (device, kernel set, grid) replayed with
+ * updated parameters (reference GraphCache, libcusort.cuh:192-225, 2693-2834).
+ * Per host thread.  Returns the previous mode. */
+int cusort_set_launch_mode(int mode);
+
+/* Device status word of the last sort that used this temp storage:
+ * 0 = ok, bit 0 = a lookback wait timed out, bit 1 = a tile-copy wait timed
+ * out.  Synchronises `stream`. */
+cudaError_t cusort_read_device_status(const void* d_temp_storage, uint32_t* status, cudaStream_t stream);
+
+/* Bound on every device-side wait, in nanoseconds (default 2e9).  Per host
+ * thread.  Returns the previous value. */
+uint64_t cusort_set_wait_limit_ns(uint64_t ns);
+
+/* Fault injection for tests: tile `tile` of every pass never publishes its
+ * lookback descriptors (-1 = off, the default).  Per host thread. */
+int64_t cusort_debug_set_skip_tile(int64_t tile);
+
+/* Per-kernel timing for the benchmark: when enabled, every sort records CUDA
+ * events around each of its kernels on `stream`; cusort_get_kernel_times
+ * synchronises on the last event and returns the durations (ms) of the last
+ * sort in launch order with kind codes 0 = init, 1 = histogram,
+ * 2 = onesweep.  Per host thread. */
+int cusort_set_kernel_timing(int enable);
+int cusort_get_kernel_times(float* ms, int* kinds, int capacity);
+
+/* Kernel geometry chosen for a call (tile items, passes, CTAs per grid) --
+ * used by tests and the benchmark's roofline arithmetic. */
+cudaError_t cusort_query_plan(cusort_key_type key_type, size_t value_bytes, int64_t num_items, int begin_bit,
+                              int end_bit, int* passes, int* tile_items, int* onesweep_grid,
+                              int* histogram_grid, int* offset_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUSORT_B200_H */

@@ -1,0 +1,664 @@
+// cusort_api.cu -- host dispatcher and C ABI of the B200 radix sort.
+//
+// Reference counterparts: DeviceRadixSort::DispatchSort (libcusort.cuh:2896-2965),
+// DispatchRadixSort::Dispatch/Invoke (libcusort.cuh:2553-2872), GraphCache
+// (libcusort.cuh:192-225) and the cached device queries of utils
+// (libcusort.cuh:227-312).  Differences by design:
+//   * device queries and occupancy are cached per (device, kernel), thread-safe;
+//   * only the control block, digit histogram and lookback descriptors are
+//     zeroed (never the staging buffers of the in/out-pointer form);
+//   * kernels are chained with programmatic dependent launch (PDL), either as
+//     direct cudaLaunchKernelEx launches or as a cached CUDA graph whose edges
+//     are programmatic;
+//   * onesweep grids are persistent (SMs x resident CTAs) with a tile ticket.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <utility>
+#include <vector>
+
+#include "../../include/cusort_b200.h"
+#include "cusort_dispatch.h"
+#include "cusort_types.h"
+
+#define CUSORT_TRY(x)                     \
+  do {                                    \
+    cudaError_t e__ = (x);                \
+    if (e__ != cudaSuccess) return e__;   \
+  } while (0)
+
+namespace cusort_b200 {
+
+// ---------------------------------------------------------------------------
+// per-device caches (thread-safe)
+// ---------------------------------------------------------------------------
+struct DeviceCache {
+  std::mutex mu;
+  std::map<int, int> sm_count;
+  std::map<std::pair<int, const void*>, int> occupancy;
+};
+static DeviceCache& dcache() {
+  static DeviceCache* c = new DeviceCache();  // never destroyed: safe at exit
+  return *c;
+}
+
+static cudaError_t get_sm_count(int dev, int* out) {
+  DeviceCache& c = dcache();
+  std::lock_guard<std::mutex> lk(c.mu);
+  auto it = c.sm_count.find(dev);
+  if (it != c.sm_count.end()) {
+    *out = it->second;
+    return cudaSuccess;
+  }
+  int v = 0;
+  CUSORT_TRY(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+  c.sm_count[dev] = v;
+  *out = v;
+  return cudaSuccess;
+}
+
+// Resident CTAs per SM for `k`; raises the kernel's dynamic shared-memory
+// limit on first use on this device.
+static cudaError_t get_occupancy(int dev, const KernelInfo& k, int* out) {
+  DeviceCache& c = dcache();
+  std::lock_guard<std::mutex> lk(c.mu);
+  auto key = std::make_pair(dev, k.func);
+  auto it = c.occupancy.find(key);
+  if (it != c.occupancy.end()) {
+    *out = it->second;
+    return cudaSuccess;
+  }
+  if (k.smem > 48 * 1024)
+    CUSORT_TRY(cudaFuncSetAttribute(k.func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem));
+  int occ = 0;
+  CUSORT_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k.func, k.threads, k.smem));
+  if (occ < 1) return cudaErrorInvalidConfiguration;
+  c.occupancy[key] = occ;
+  *out = occ;
+  return cudaSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// key traits
+// ---------------------------------------------------------------------------
+static int key_bytes_of(int kt) {
+  switch (kt) {
+    case CUSORT_KEY_U8: case CUSORT_KEY_I8: return 1;
+    case CUSORT_KEY_U16: case CUSORT_KEY_I16: return 2;
+    case CUSORT_KEY_U32: case CUSORT_KEY_I32: case CUSORT_KEY_F32: return 4;
+    case CUSORT_KEY_U64: case CUSORT_KEY_I64: case CUSORT_KEY_F64: return 8;
+    default: return 0;
+  }
+}
+static bool value_bytes_ok(size_t vb) { return vb == 1 || vb == 2 || vb == 4 || vb == 8 || vb == 16; }
+
+// Twiddle constants (C, F) of dev::twiddle; reference RadixTraits::Twiddle
+// (libcusort.cuh:417-429).
+static void twiddle_constants(int kt, int kb, bool desc, uint64_t* c, uint64_t* f) {
+  const uint64_t all = (kb == 8) ? ~0ull : ((1ull << (8 * kb)) - 1);
+  const uint64_t sb = 1ull << (8 * kb - 1);
+  const bool is_float = kt == CUSORT_KEY_F32 || kt == CUSORT_KEY_F64;
+  const bool is_signed = kt == CUSORT_KEY_I8 || kt == CUSORT_KEY_I16 || kt == CUSORT_KEY_I32 || kt == CUSORT_KEY_I64;
+  uint64_t cc = 0, ff = 0;
+  if (is_float) {
+    cc = sb;
+    ff = all ^ sb;
+  } else if (is_signed) {
+    cc = sb;
+  }
+  if (desc) cc ^= all;
+  *c = cc;
+  *f = ff;
+}
+
+// ---------------------------------------------------------------------------
+// plan: kernels, grids and temp-storage layout
+//   [control 256 B: status u32 @0, tile counters u32[8] @64]
+//   [digit histogram: passes x 256 x OffsetT]
+//   [lookback descriptors: tiles x 256 x OffsetT]     <- zeroed by init
+//   [staging keys n x K][staging values n x V]        <- in/out form, passes >= 2
+// ---------------------------------------------------------------------------
+struct Plan {
+  int kt = 0, kb = 0, vb = 0, offb = 4;
+  bool desc = false;
+  uint64_t n = 0;
+  int begin = 0, end = 0;
+  uint32_t passes = 0, last_mask = 0;
+  uint64_t tw_c = 0, tw_f = 0;
+  KernelInfo os, hist;
+  uint64_t tiles = 0;
+  size_t off_hist = 0, off_desc = 0, off_stage_k = 0, off_stage_v = 0, zero_bytes = 0, total = 0;
+  bool staging = false;
+};
+
+constexpr size_t kCtrlBytes = 256;
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int end, bool raw, Plan* p) {
+  p->kt = kt;
+  p->kb = key_bytes_of(kt);
+  p->vb = (int)vb;
+  p->desc = desc;
+  p->n = n;
+  p->begin = begin;
+  p->end = end;
+  // 30 count bits per descriptor word with 32-bit offsets (2 state bits).
+  p->offb = (n < (1ull << 30)) ? 4 : 8;
+  const uint32_t nbits = (uint32_t)(end - begin);
+  p->passes = (nbits + kRadixBits - 1) / kRadixBits;
+  p->last_mask = (1u << (nbits - (p->passes - 1) * kRadixBits)) - 1u;
+  twiddle_constants(kt, p->kb, desc, &p->tw_c, &p->tw_f);
+  bool ok = false;
+  switch (p->kb) {
+    case 1: ok = get_kernels_k1(p->vb, p->offb, &p->os, &p->hist); break;
+    case 2: ok = get_kernels_k2(p->vb, p->offb, &p->os, &p->hist); break;
+    case 4: ok = get_kernels_k4(p->vb, p->offb, &p->os, &p->hist); break;
+    case 8: ok = get_kernels_k8(p->vb, p->offb, &p->os, &p->hist); break;
+    default: ok = false;
+  }
+  if (!ok) return false;
+  p->tiles = (n + p->os.tile - 1) / p->os.tile;
+  p->off_hist = kCtrlBytes;
+  p->off_desc = p->off_hist + align256((size_t)p->passes * kRadix * p->offb);
+  const size_t end_desc = p->off_desc + align256((size_t)p->tiles * kRadix * p->offb);
+  p->zero_bytes = end_desc;
+  p->staging = raw && p->passes >= 2;
+  p->off_stage_k = end_desc;
+  p->off_stage_v = p->off_stage_k + (p->staging ? align256((size_t)n * p->kb) : 0);
+  p->total = p->off_stage_v + ((p->staging && p->vb) ? align256((size_t)n * p->vb) : 0);
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// per-thread settings, timing and graph cache
+// ---------------------------------------------------------------------------
+struct GraphEntry {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::vector<cudaGraphNode_t> nodes;  // init, histogram, onesweep[0..P-1]
+};
+using GraphKey = std::tuple<int, const void*, const void*, uint32_t, int, int, int>;
+
+struct ThreadState {
+  int launch_mode = 0;
+  uint64_t wait_limit_ns = 2000000000ull;
+  int64_t skip_tile = -1;
+  int timing = 0;
+  std::vector<cudaEvent_t> events;
+  std::vector<int> kinds;
+  int recorded = 0;
+  std::map<GraphKey, GraphEntry> graphs;
+  ~ThreadState() {
+    // Best effort: the CUDA context may already be gone at process exit.
+    for (auto& kv : graphs) {
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+      if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+    }
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+  }
+};
+static thread_local ThreadState g_ts;
+
+static void timing_begin(cudaStream_t s, int kind) {
+  if (!g_ts.timing) return;
+  const size_t need = (size_t)(g_ts.recorded + 1) * 2;
+  while (g_ts.events.size() < need) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return;
+    g_ts.events.push_back(e);
+  }
+  if ((int)g_ts.kinds.size() <= g_ts.recorded) g_ts.kinds.resize(g_ts.recorded + 1);
+  g_ts.kinds[g_ts.recorded] = kind;
+  cudaEventRecord(g_ts.events[2 * g_ts.recorded], s);
+}
+static void timing_end(cudaStream_t s) {
+  if (!g_ts.timing) return;
+  if ((size_t)(2 * g_ts.recorded + 1) >= g_ts.events.size()) return;
+  cudaEventRecord(g_ts.events[2 * g_ts.recorded + 1], s);
+  g_ts.recorded++;
+}
+
+// ---------------------------------------------------------------------------
+// launch sequence
+// ---------------------------------------------------------------------------
+struct Launch {
+  const void* func;
+  int grid, threads;
+  size_t smem;
+  bool pdl;
+  int kind;
+  union {
+    InitArgs init;
+    HistArgs hist;
+    OnesweepArgs os;
+  } args;
+};
+
+struct PassBuffers {
+  const void* k_src[kMaxPasses];
+  void* k_dst[kMaxPasses];
+  const void* v_src[kMaxPasses];
+  void* v_dst[kMaxPasses];
+};
+
+static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers& b, std::vector<Launch>* out) {
+  int dev = 0;
+  CUSORT_TRY(cudaGetDevice(&dev));
+  int sms = 0, occ_os = 0, occ_h = 0;
+  CUSORT_TRY(get_sm_count(dev, &sms));
+  CUSORT_TRY(get_occupancy(dev, p.os, &occ_os));
+  CUSORT_TRY(get_occupancy(dev, p.hist, &occ_h));
+
+  uint8_t* t = static_cast<uint8_t*>(d_temp);
+  uint32_t* status = reinterpret_cast<uint32_t*>(t);
+  uint32_t* counters = reinterpret_cast<uint32_t*>(t + 64);
+  uint8_t* g_hist = t + p.off_hist;
+  void* desc = t + p.off_desc;
+
+  out->clear();
+  {
+    Launch l{};
+    l.func = get_init_kernel();
+    const uint64_t n16 = p.zero_bytes / 16;
+    l.grid = (int)std::min<uint64_t>((uint64_t)sms * 4, std::max<uint64_t>(1, (n16 + 511) / 512));
+    l.threads = 512;
+    l.smem = 0;
+    l.pdl = false;  // first kernel: full ordering after the caller's work
+    l.kind = 0;
+    l.args.init.ptr = d_temp;
+    l.args.init.n16 = n16;
+    out->push_back(l);
+  }
+  {
+    Launch l{};
+    l.func = p.hist.func;
+    const uint64_t vec = p.n * p.kb / 16 + 1;
+    const uint64_t want = (vec + p.hist.tile - 1) / p.hist.tile;
+    l.grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ_h, want));
+    l.threads = p.hist.threads;
+    l.smem = 0;
+    l.pdl = true;
+    l.kind = 1;
+    HistArgs& h = l.args.hist;
+    h.keys = b.k_src[0];
+    h.n = p.n;
+    h.tw_c = p.tw_c;
+    h.tw_f = p.tw_f;
+    h.begin_bit = (uint32_t)p.begin;
+    h.num_passes = p.passes;
+    h.last_mask = p.last_mask;
+    h.g_hist = g_hist;
+    out->push_back(l);
+  }
+  const int os_grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ_os, p.tiles));
+  for (uint32_t pass = 0; pass < p.passes; ++pass) {
+    Launch l{};
+    l.func = p.os.func;
+    l.grid = os_grid;
+    l.threads = p.os.threads;
+    l.smem = p.os.smem;
+    l.pdl = true;
+    l.kind = 2;
+    OnesweepArgs& a = l.args.os;
+    a.keys_in = b.k_src[pass];
+    a.keys_out = b.k_dst[pass];
+    a.vals_in = p.vb ? b.v_src[pass] : nullptr;
+    a.vals_out = p.vb ? b.v_dst[pass] : nullptr;
+    a.n = p.n;
+    a.tw_c = p.tw_c;
+    a.tw_f = p.tw_f;
+    a.shift = (uint32_t)p.begin + pass * kRadixBits;
+    a.mask = (pass + 1 == p.passes) ? p.last_mask : 0xffu;
+    a.pass = pass;
+    a.num_tiles = (uint32_t)p.tiles;
+    a.desc = desc;
+    a.g_hist_pass = g_hist + (size_t)pass * kRadix * p.offb;
+    a.tile_counter = counters + pass;
+    a.status = status;
+    a.spin_limit_ns = g_ts.wait_limit_ns;
+    a.skip_tile = g_ts.skip_tile;
+    const size_t tile_k = (size_t)p.os.tile * p.kb, tile_v = (size_t)p.os.tile * p.vb;
+    a.tma_keys = ((reinterpret_cast<uintptr_t>(a.keys_in) & 15) == 0 && (tile_k & 15) == 0) ? 1u : 0u;
+    a.tma_vals = (p.vb == 0 || ((reinterpret_cast<uintptr_t>(a.vals_in) & 15) == 0 && (tile_v & 15) == 0)) ? 1u : 0u;
+    out->push_back(l);
+  }
+  return cudaSuccess;
+}
+
+static cudaError_t launch_direct(const std::vector<Launch>& ls, cudaStream_t stream) {
+  g_ts.recorded = 0;
+  for (const Launch& l : ls) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)l.grid);
+    cfg.blockDim = dim3((unsigned)l.threads);
+    cfg.dynamicSmemBytes = l.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (l.pdl && !g_ts.timing) {
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+    }
+    void* args[1] = {const_cast<void*>(static_cast<const void*>(&l.args))};
+    timing_begin(stream, l.kind);
+    CUSORT_TRY(cudaLaunchKernelExC(&cfg, l.func, args));
+    timing_end(stream);
+  }
+  return cudaSuccess;
+}
+
+static cudaKernelNodeParams node_params(const Launch& l, void** argv) {
+  cudaKernelNodeParams kp = {};
+  kp.func = const_cast<void*>(l.func);
+  kp.gridDim = dim3((unsigned)l.grid);
+  kp.blockDim = dim3((unsigned)l.threads);
+  kp.sharedMemBytes = (unsigned)l.smem;
+  argv[0] = const_cast<void*>(static_cast<const void*>(&l.args));
+  kp.kernelParams = argv;
+  kp.extra = nullptr;
+  return kp;
+}
+
+// Graph mode: one graph per (device, kernels, passes, grids) and host thread,
+// built once with programmatic edges, then replayed after updating every
+// kernel node's arguments (reference GraphCache, libcusort.cuh:2693-2834).
+static cudaError_t launch_graph(const std::vector<Launch>& ls, cudaStream_t stream) {
+  int dev = 0;
+  CUSORT_TRY(cudaGetDevice(&dev));
+  const GraphKey key{dev, ls[1].func, ls.back().func, (uint32_t)ls.size(), ls[0].grid, ls[1].grid, ls.back().grid};
+  auto it = g_ts.graphs.find(key);
+  if (it == g_ts.graphs.end()) {
+    GraphEntry ge;
+    CUSORT_TRY(cudaGraphCreate(&ge.graph, 0));
+    cudaGraphNode_t prev = nullptr;
+    for (const Launch& l : ls) {
+      void* argv[1];
+      cudaKernelNodeParams kp = node_params(l, argv);
+      cudaGraphNode_t node;
+      cudaError_t e = cudaGraphAddKernelNode(&node, ge.graph, nullptr, 0, &kp);
+      if (e == cudaSuccess && prev) {
+        cudaGraphEdgeData ed = {};
+        ed.from_port = l.pdl ? cudaGraphKernelNodePortProgrammatic : cudaGraphKernelNodePortDefault;
+        ed.type = l.pdl ? cudaGraphDependencyTypeProgrammatic : cudaGraphDependencyTypeDefault;
+        e = cudaGraphAddDependencies_v2(ge.graph, &prev, &node, &ed, 1);
+      }
+      if (e != cudaSuccess) {
+        cudaGraphDestroy(ge.graph);
+        return e;
+      }
+      ge.nodes.push_back(node);
+      prev = node;
+    }
+    cudaError_t e = cudaGraphInstantiate(&ge.exec, ge.graph, 0);
+    if (e != cudaSuccess) {
+      cudaGraphDestroy(ge.graph);
+      return e;
+    }
+    it = g_ts.graphs.emplace(key, std::move(ge)).first;
+  }
+  GraphEntry& ge = it->second;
+  for (size_t i = 0; i < ls.size(); ++i) {
+    void* argv[1];
+    cudaKernelNodeParams kp = node_params(ls[i], argv);
+    CUSORT_TRY(cudaGraphExecKernelNodeSetParams(ge.exec, ge.nodes[i], &kp));
+  }
+  return cudaGraphLaunch(ge.exec, stream);
+}
+
+// ---------------------------------------------------------------------------
+// DispatchSort equivalent
+// ---------------------------------------------------------------------------
+struct SortCall {
+  void* d_temp;
+  size_t* temp_bytes;
+  int kt;
+  size_t vb;  // 0 = keys only
+  bool desc;
+  bool raw;
+  // raw form
+  const void* k_in;
+  void* k_out;
+  const void* v_in;
+  void* v_out;
+  // DoubleBuffer form
+  cusort_double_buffer* kdb;
+  cusort_double_buffer* vdb;
+  int64_t n;
+  int begin, end;
+  cudaStream_t stream;
+};
+
+static cudaError_t sort_impl(const SortCall& c) {
+  const int kb = key_bytes_of(c.kt);
+  if (kb == 0 || c.temp_bytes == nullptr) return cudaErrorInvalidValue;
+  if (c.vb != 0 && !value_bytes_ok(c.vb)) return cudaErrorInvalidValue;
+  if (c.begin < 0 || c.end < 0 || c.begin > c.end || c.end > 8 * kb) return cudaErrorInvalidValue;
+  if (!c.raw && (c.kdb == nullptr || (c.vb && c.vdb == nullptr))) return cudaErrorInvalidValue;
+
+  // Trivial calls (libcusort.cuh:2914-2931).
+  if (c.n <= 1 || c.begin == c.end) {
+    if (c.d_temp == nullptr) {
+      *c.temp_bytes = (c.raw && c.n > 0) ? 1 : 0;
+    } else if (c.raw && c.n > 0) {
+      CUSORT_TRY(cudaMemcpyAsync(c.k_out, c.k_in, (size_t)c.n * kb, cudaMemcpyDeviceToDevice, c.stream));
+      if (c.vb) CUSORT_TRY(cudaMemcpyAsync(c.v_out, c.v_in, (size_t)c.n * c.vb, cudaMemcpyDeviceToDevice, c.stream));
+    }
+    return cudaSuccess;
+  }
+
+  Plan p;
+  if (!make_plan(c.kt, c.vb, c.desc, (uint64_t)c.n, c.begin, c.end, c.raw, &p)) return cudaErrorInvalidValue;
+  if (c.d_temp == nullptr) {
+    *c.temp_bytes = p.total;
+    return cudaSuccess;
+  }
+  if (*c.temp_bytes < p.total) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(c.d_temp) & 15) != 0) return cudaErrorInvalidValue;
+
+  PassBuffers b = {};
+  if (c.raw) {
+    // pass p writes `out` when (P-1-p) is even, the staging buffer otherwise,
+    // so the last pass lands in `out` and `in` is never written.
+    uint8_t* t = static_cast<uint8_t*>(c.d_temp);
+    void* sk = t + p.off_stage_k;
+    void* sv = t + p.off_stage_v;
+    const void* ks = c.k_in;
+    const void* vs = c.v_in;
+    for (uint32_t i = 0; i < p.passes; ++i) {
+      const bool to_out = ((p.passes - 1 - i) & 1u) == 0;
+      b.k_src[i] = ks;
+      b.k_dst[i] = to_out ? c.k_out : sk;
+      b.v_src[i] = vs;
+      b.v_dst[i] = to_out ? c.v_out : sv;
+      ks = b.k_dst[i];
+      vs = b.v_dst[i];
+    }
+  } else {
+    int ksel = c.kdb->selector & 1, vsel = c.vb ? (c.vdb->selector & 1) : 0;
+    for (uint32_t i = 0; i < p.passes; ++i) {
+      b.k_src[i] = c.kdb->d_buffers[ksel];
+      b.k_dst[i] = c.kdb->d_buffers[ksel ^ 1];
+      if (c.vb) {
+        b.v_src[i] = c.vdb->d_buffers[vsel];
+        b.v_dst[i] = c.vdb->d_buffers[vsel ^ 1];
+      }
+      ksel ^= 1;
+      vsel ^= 1;
+    }
+  }
+
+  std::vector<Launch> ls;
+  CUSORT_TRY(build_launches(p, c.d_temp, b, &ls));
+  if (g_ts.launch_mode == 1 && !g_ts.timing)
+    CUSORT_TRY(launch_graph(ls, c.stream));
+  else
+    CUSORT_TRY(launch_direct(ls, c.stream));
+
+  if (!c.raw) {
+    c.kdb->selector ^= (int)(p.passes & 1u);
+    if (c.vb) c.vdb->selector ^= (int)(p.passes & 1u);
+  }
+  return cudaSuccess;
+}
+
+}  // namespace cusort_b200
+
+using namespace cusort_b200;
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+static cudaError_t sort_db(void* t, size_t* tb, cusort_key_type kt, cusort_double_buffer* k, size_t vb,
+                           cusort_double_buffer* v, int64_t n, int b, int e, bool desc, cudaStream_t s) {
+  SortCall c = {};
+  c.d_temp = t;
+  c.temp_bytes = tb;
+  c.kt = (int)kt;
+  c.vb = vb;
+  c.desc = desc;
+  c.raw = false;
+  c.kdb = k;
+  c.vdb = v;
+  c.n = n;
+  c.begin = b;
+  c.end = e;
+  c.stream = s;
+  return sort_impl(c);
+}
+
+static cudaError_t sort_raw(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko, size_t vb,
+                            const void* vi, void* vo, int64_t n, int b, int e, bool desc, cudaStream_t s) {
+  SortCall c = {};
+  c.d_temp = t;
+  c.temp_bytes = tb;
+  c.kt = (int)kt;
+  c.vb = vb;
+  c.desc = desc;
+  c.raw = true;
+  c.k_in = ki;
+  c.k_out = ko;
+  c.v_in = vi;
+  c.v_out = vo;
+  c.n = n;
+  c.begin = b;
+  c.end = e;
+  c.stream = s;
+  return sort_impl(c);
+}
+
+cudaError_t cusort_sort_keys_db(void* t, size_t* tb, cusort_key_type kt, cusort_double_buffer* k, int64_t n, int b,
+                                int e, cudaStream_t s) {
+  return sort_db(t, tb, kt, k, 0, nullptr, n, b, e, false, s);
+}
+cudaError_t cusort_sort_keys_descending_db(void* t, size_t* tb, cusort_key_type kt, cusort_double_buffer* k,
+                                           int64_t n, int b, int e, cudaStream_t s) {
+  return sort_db(t, tb, kt, k, 0, nullptr, n, b, e, true, s);
+}
+cudaError_t cusort_sort_pairs_db(void* t, size_t* tb, cusort_key_type kt, cusort_double_buffer* k, size_t vb,
+                                 cusort_double_buffer* v, int64_t n, int b, int e, cudaStream_t s) {
+  if (vb == 0) return cudaErrorInvalidValue;
+  return sort_db(t, tb, kt, k, vb, v, n, b, e, false, s);
+}
+cudaError_t cusort_sort_pairs_descending_db(void* t, size_t* tb, cusort_key_type kt, cusort_double_buffer* k,
+                                            size_t vb, cusort_double_buffer* v, int64_t n, int b, int e,
+                                            cudaStream_t s) {
+  if (vb == 0) return cudaErrorInvalidValue;
+  return sort_db(t, tb, kt, k, vb, v, n, b, e, true, s);
+}
+cudaError_t cusort_sort_keys(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko, int64_t n, int b,
+                             int e, cudaStream_t s) {
+  return sort_raw(t, tb, kt, ki, ko, 0, nullptr, nullptr, n, b, e, false, s);
+}
+cudaError_t cusort_sort_keys_descending(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko,
+                                        int64_t n, int b, int e, cudaStream_t s) {
+  return sort_raw(t, tb, kt, ki, ko, 0, nullptr, nullptr, n, b, e, true, s);
+}
+cudaError_t cusort_sort_pairs(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko, size_t vb,
+                              const void* vi, void* vo, int64_t n, int b, int e, cudaStream_t s) {
+  if (vb == 0) return cudaErrorInvalidValue;
+  return sort_raw(t, tb, kt, ki, ko, vb, vi, vo, n, b, e, false, s);
+}
+cudaError_t cusort_sort_pairs_descending(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko,
+                                         size_t vb, const void* vi, void* vo, int64_t n, int b, int e,
+                                         cudaStream_t s) {
+  if (vb == 0) return cudaErrorInvalidValue;
+  return sort_raw(t, tb, kt, ki, ko, vb, vi, vo, n, b, e, true, s);
+}
+
+const char* cusort_version(void) { return "1.0.1-b200.1"; }
+
+int cusort_set_launch_mode(int mode) {
+  const int prev = g_ts.launch_mode;
+  if (mode == 0 || mode == 1) g_ts.launch_mode = mode;
+  return prev;
+}
+
+cudaError_t cusort_read_device_status(const void* d_temp_storage, uint32_t* status, cudaStream_t stream) {
+  if (d_temp_storage == nullptr || status == nullptr) return cudaErrorInvalidValue;
+  CUSORT_TRY(cudaMemcpyAsync(status, d_temp_storage, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+  return cudaStreamSynchronize(stream);
+}
+
+uint64_t cusort_set_wait_limit_ns(uint64_t ns) {
+  const uint64_t prev = g_ts.wait_limit_ns;
+  if (ns > 0) g_ts.wait_limit_ns = ns;
+  return prev;
+}
+
+int64_t cusort_debug_set_skip_tile(int64_t tile) {
+  const int64_t prev = g_ts.skip_tile;
+  g_ts.skip_tile = tile;
+  return prev;
+}
+
+int cusort_set_kernel_timing(int enable) {
+  const int prev = g_ts.timing;
+  g_ts.timing = enable ? 1 : 0;
+  return prev;
+}
+
+int cusort_get_kernel_times(float* ms, int* kinds, int capacity) {
+  const int n = g_ts.recorded;
+  if (n == 0) return 0;
+  if (cudaEventSynchronize(g_ts.events[2 * n - 1]) != cudaSuccess) return -1;
+  const int m = std::min(n, capacity);
+  for (int i = 0; i < m; ++i) {
+    float v = 0.f;
+    cudaEventElapsedTime(&v, g_ts.events[2 * i], g_ts.events[2 * i + 1]);
+    if (ms) ms[i] = v;
+    if (kinds) kinds[i] = g_ts.kinds[i];
+  }
+  return m;
+}
+
+cudaError_t cusort_query_plan(cusort_key_type kt, size_t vb, int64_t n, int begin, int end, int* passes,
+                              int* tile_items, int* onesweep_grid, int* histogram_grid, int* offset_bytes) {
+  const int kb = key_bytes_of((int)kt);
+  if (kb == 0 || (vb != 0 && !value_bytes_ok(vb)) || n < 2 || begin < 0 || begin >= end || end > 8 * kb)
+    return cudaErrorInvalidValue;
+  Plan p;
+  if (!make_plan((int)kt, vb, false, (uint64_t)n, begin, end, false, &p)) return cudaErrorInvalidValue;
+  if (passes) *passes = (int)p.passes;
+  if (tile_items) *tile_items = p.os.tile;
+  if (offset_bytes) *offset_bytes = p.offb;
+  if (onesweep_grid || histogram_grid) {
+    int dev = 0, sms = 0, occ_os = 0, occ_h = 0;
+    CUSORT_TRY(cudaGetDevice(&dev));
+    CUSORT_TRY(get_sm_count(dev, &sms));
+    CUSORT_TRY(get_occupancy(dev, p.os, &occ_os));
+    CUSORT_TRY(get_occupancy(dev, p.hist, &occ_h));
+    if (onesweep_grid) *onesweep_grid = (int)std::min<uint64_t>((uint64_t)sms * occ_os, p.tiles);
+    if (histogram_grid) *histogram_grid = sms * occ_h;
+  }
+  return cudaSuccess;
+}
+
+}  // extern "C"

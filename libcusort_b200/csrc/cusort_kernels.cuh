@@ -1,0 +1,372 @@
+// cusort_kernels.cuh -- the three kernels of one sort, as templates.
+//
+//   init_kernel       zero the control block + lookback descriptors
+//   histogram_kernel  one read of the keys -> digit counts of every pass
+//   onesweep_kernel   one stable 8-bit LSD pass (persistent CTAs, TMA tile
+//                     staging, shared-memory ranking, decoupled lookback,
+//                     shared-memory reorder, coalesced scatter)
+//
+// Reference counterparts: RadixSortHistogramKernel (libcusort.cuh:1679-1841),
+// RadixSortOnesweepKernel (libcusort.cuh:1843-2415), the temp memset
+// (libcusort.cuh:2650).  The algorithm (Onesweep: one upfront histogram, one
+// binning kernel per digit with decoupled lookback) is the same; the kernels
+// are re-designed for sm_100a (see the per-kernel comments).
+#pragma once
+
+#include "cusort_device.cuh"
+
+namespace cusort_b200 {
+
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---------------------------------------------------------------------------
+// histogram: digit counts of every pass from ONE read of the keys.
+// 16-byte streaming loads (ld.global.nc.L1::no_allocate.v4), UNROLL vectors in
+// flight per thread, per-CTA shared-memory counters, one global atomic per
+// (pass, digit) per CTA.  The global atomics wait for the init kernel (PDL);
+// the key reads and shared-memory counting overlap it.
+// ---------------------------------------------------------------------------
+template <int KB, typename Off, int THREADS, int UNROLL>
+__global__ void __launch_bounds__(THREADS) histogram_kernel(const HistArgs a) {
+  using K = typename dev::UIntOf<KB>::T;
+  constexpr int MAXP = KB;            // 8-bit digits: at most one pass per key byte
+  constexpr int PER = 16 / KB;        // keys per 16-byte vector
+  __shared__ uint32_t s_hist[MAXP * kRadix];
+
+  dev::pdl_launch_dependents();
+  const uint32_t tid = threadIdx.x;
+  for (uint32_t i = tid; i < MAXP * kRadix; i += THREADS) s_hist[i] = 0;
+  __syncthreads();
+
+  const K tc = (K)a.tw_c, tf = (K)a.tw_f;
+  const uint32_t P = a.num_passes;
+  auto count = [&](K k) {
+    const K t = dev::twiddle<K>(k, tc, tf);
+#pragma unroll
+    for (int p = 0; p < MAXP; ++p) {
+      if (p < (int)P) {
+        const uint32_t m = (p + 1 == (int)P) ? a.last_mask : 0xffu;
+        const uint32_t d = (uint32_t)(t >> (a.begin_bit + 8 * p)) & m;
+        atomicAdd(&s_hist[p * kRadix + d], 1u);
+      }
+    }
+  };
+
+  const K* keys = static_cast<const K*>(a.keys);
+  const uint64_t n = a.n;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(keys);
+  uint64_t head = ((16 - (addr & 15)) & 15) / KB;
+  if (head > n) head = n;
+  const uint64_t nvec = (n - head) / PER;
+  const uint4* vec = reinterpret_cast<const uint4*>(keys + head);
+  const uint64_t gthreads = (uint64_t)gridDim.x * THREADS;
+  const uint64_t gtid = (uint64_t)blockIdx.x * THREADS + tid;
+
+  uint64_t v = gtid;
+  for (; v + (UNROLL - 1) * gthreads < nvec; v += UNROLL * gthreads) {
+    uint4 x[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) x[u] = dev::ld_stream_v4(vec + v + u * gthreads);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const K* kk = reinterpret_cast<const K*>(&x[u]);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) count(kk[e]);
+    }
+  }
+  for (; v < nvec; v += gthreads) {
+    uint4 x = dev::ld_stream_v4(vec + v);
+    const K* kk = reinterpret_cast<const K*>(&x);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) count(kk[e]);
+  }
+  // Unaligned head and ragged tail, element by element.
+  for (uint64_t i = gtid; i < head; i += gthreads) count(keys[i]);
+  for (uint64_t i = head + nvec * PER + gtid; i < n; i += gthreads) count(keys[i]);
+  __syncthreads();
+
+  dev::pdl_wait();  // g_hist zeroed by init_kernel
+  Off* g = static_cast<Off*>(a.g_hist);
+  for (uint32_t i = tid; i < P * kRadix; i += THREADS) {
+    const uint32_t c = s_hist[i];
+    if (c) atomicAdd(g + i, (Off)c);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// onesweep: one stable LSD pass over digit (shift, mask).
+//
+// Persistent CTAs take tiles from a global ticket counter (so the lookback
+// only ever waits on tiles that a running CTA already owns).  Per tile:
+//   1. TMA bulk copy of the tile's keys (and values) into shared memory
+//      (cooperative loads for the ragged last tile or unaligned pointers);
+//   2. each warp ranks its 32*KPT keys slot by slot with the shared-memory
+//      match (dev::warp_rank_slot), keys/values held in registers;
+//   3. per-digit counts -> aggregate descriptor published at once; tile-local
+//      exclusive digit offsets by a 256-wide block scan;
+//   4. keys/values are written back to shared memory in sorted order;
+//   5. decoupled lookback over earlier tiles' descriptors (bounded wait), the
+//      inclusive descriptor is published;
+//   6. coalesced global scatter: consecutive threads write consecutive
+//      positions of each digit run.
+// Out-of-range slots of the last tile take the top digit and are never
+// written (their sorted positions are >= the tile's valid count).
+// ---------------------------------------------------------------------------
+template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_>
+struct OnesweepCfg {
+  static constexpr int KB = KB_, VB = VB_, THREADS = THREADS_, KPT = KPT_, MINB = MINB_;
+  using Off = Off_;
+  static constexpr int WARPS = THREADS / 32;
+  static constexpr int TILE = THREADS * KPT;
+  static constexpr size_t OFF_KEYS = 0;
+  static constexpr size_t OFF_VALS = align_up(OFF_KEYS + (size_t)TILE * KB, 128);
+  static constexpr size_t OFF_WTAB = align_up(OFF_VALS + (size_t)TILE * VB, 128);
+  static constexpr size_t OFF_TSTART = OFF_WTAB + (size_t)WARPS * kRadix * 8;
+  static constexpr size_t OFF_GBASE = OFF_TSTART + kRadix * 4;
+  static constexpr size_t OFF_GOFF = OFF_GBASE + kRadix * sizeof(Off);
+  static constexpr size_t OFF_MISC = OFF_GOFF + kRadix * sizeof(Off);
+  static constexpr size_t OFF_MBAR = OFF_MISC + 16 * 4;
+  static constexpr size_t SMEM_BYTES = OFF_MBAR + 16;
+  static_assert(THREADS >= kRadix && THREADS % 32 == 0, "need >= 256 threads");
+  static_assert(TILE * (KB + VB) < (1 << 20), "mbarrier tx-count limit");
+  static_assert(32 * KPT < (1 << 24), "rank packing");
+};
+
+constexpr int kLookbackWindow = 8;
+
+template <typename Off>
+struct DescBits {
+  static constexpr int SH = sizeof(Off) * 8 - 2;
+  static constexpr Off COUNT_MASK = (Off(1) << SH) - 1;
+  __device__ __forceinline__ static Off make(uint32_t pass, uint32_t state, Off count) {
+    return (Off((2u * pass + state) & 3u) << SH) | count;
+  }
+  __device__ __forceinline__ static uint32_t state(Off w, uint32_t pass) {
+    return ((uint32_t)(w >> SH) - 2u * pass) & 3u;
+  }
+};
+
+// Exclusive prefix over earlier tiles of this digit's counts (decoupled
+// lookback; reference LookbackComputePrefixAndPublishComplete,
+// libcusort.cuh:1340-1382, walks one tile per L2 round trip).  Here each
+// digit's thread reads a window of W predecessor words per round trip
+// (independent loads), adds aggregates from the nearest outward and stops at
+// the first INCLUSIVE word; an EMPTY word ends the window and is re-polled
+// (bounded wait).  Tile 0 has no predecessors.
+template <typename Off, int W>
+__device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, uint32_t digit, uint32_t pass,
+                                               uint32_t* status, uint64_t limit_ns) {
+  using DB = DescBits<Off>;
+  Off excl = 0;
+  int64_t j = (int64_t)tile - 1;  // nearest predecessor not yet accounted for
+  dev::SpinGuard guard;
+  while (j >= 0) {
+    Off w[W];
+#pragma unroll
+    for (int k = 0; k < W; ++k)
+      w[k] = (j - k >= 0) ? dev::ld_relaxed(desc + (size_t)(j - k) * kRadix + digit)
+                          : DB::make(pass, kDescInclusive, Off(0));
+    int consumed = 0;
+    bool done = false;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      if (done || consumed < k) continue;  // stopped earlier in this window
+      const uint32_t st = DB::state(w[k], pass);
+      if (st == kDescEmpty) continue;
+      excl += w[k] & DB::COUNT_MASK;
+      consumed = k + 1;
+      done = (st == kDescInclusive);
+    }
+    if (done) break;
+    j -= consumed;
+    if (consumed == 0 && guard.expired(status, limit_ns)) {
+      atomicOr(status, kStatusLookbackTimeout);
+      break;
+    }
+  }
+  return excl;
+}
+
+template <class CFG>
+__global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const OnesweepArgs a) {
+  using K = typename dev::UIntOf<CFG::KB>::T;
+  using V = typename dev::UIntOf<(CFG::VB ? CFG::VB : 1)>::T;
+  using Off = typename CFG::Off;
+  using DB = DescBits<Off>;
+  constexpr int THREADS = CFG::THREADS, KPT = CFG::KPT, TILE = CFG::TILE, WARPS = CFG::WARPS;
+  constexpr bool HAS_V = CFG::VB > 0;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  K* s_keys = reinterpret_cast<K*>(smem + CFG::OFF_KEYS);
+  V* s_vals = reinterpret_cast<V*>(smem + CFG::OFF_VALS);
+  unsigned long long* s_wtab = reinterpret_cast<unsigned long long*>(smem + CFG::OFF_WTAB);
+  uint32_t* s_tstart = reinterpret_cast<uint32_t*>(smem + CFG::OFF_TSTART);
+  Off* s_gbase = reinterpret_cast<Off*>(smem + CFG::OFF_GBASE);
+  Off* s_goff = reinterpret_cast<Off*>(smem + CFG::OFF_GOFF);
+  uint32_t* s_misc = reinterpret_cast<uint32_t*>(smem + CFG::OFF_MISC);  // [0] ticket [1] abort [2..9] scan
+  uint64_t* s_mbar = reinterpret_cast<uint64_t*>(smem + CFG::OFF_MBAR);
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const K tc = (K)a.tw_c, tf = (K)a.tw_f;
+  const K* keys_in = static_cast<const K*>(a.keys_in);
+  K* keys_out = static_cast<K*>(a.keys_out);
+  const V* vals_in = static_cast<const V*>(a.vals_in);
+  V* vals_out = static_cast<V*>(a.vals_out);
+  Off* desc = static_cast<Off*>(a.desc);
+
+  if (tid == 0) {
+    dev::mbar_init(s_mbar, 1);
+    dev::fence_mbar_init();
+    s_misc[1] = 0;
+  }
+  dev::pdl_wait();
+  dev::pdl_launch_dependents();
+
+  // Global exclusive offset of every digit for this pass (from the upfront
+  // histogram), computed once per CTA.
+  {
+    uint32_t c = 0;
+    if (tid < kRadix) c = (uint32_t)static_cast<const Off*>(a.g_hist_pass)[tid];
+    // 64-bit totals can exceed 32 bits only for n > 2^32; scan in Off.
+    Off cv = (tid < kRadix) ? static_cast<const Off*>(a.g_hist_pass)[tid] : Off(0);
+    (void)c;
+    Off incl = cv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      Off t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= (uint32_t)o) incl += t;
+    }
+    if (lane == 31 && warp < 8) s_goff[warp] = incl;
+    __syncthreads();
+    if (tid < kRadix) {
+      Off pre = 0;
+      for (uint32_t w = 0; w < warp; ++w) pre += s_goff[w];
+      s_gbase[tid] = pre + incl - cv;
+    }
+    __syncthreads();
+  }
+
+  const uint64_t pol = dev::l2_policy_evict_first();
+  uint32_t phase = 0;
+  const uint32_t lt = dev::lanemask_lt();
+  unsigned long long* wt = s_wtab + warp * kRadix;
+
+  for (;;) {
+    if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
+#pragma unroll
+    for (int i = 0; i < kRadix / 32; ++i) wt[lane + 32 * i] = 0ull;
+    __syncthreads();
+    const uint32_t tile = s_misc[0];
+    if (tile >= a.num_tiles) break;
+    const uint64_t base = (uint64_t)tile * TILE;
+    const uint32_t valid = (uint32_t)((a.n - base) < (uint64_t)TILE ? (a.n - base) : (uint64_t)TILE);
+    const bool publish = (int64_t)tile != a.skip_tile;
+
+    // ---- 1. stage the tile in shared memory
+    if (valid == (uint32_t)TILE && a.tma_keys && (!HAS_V || a.tma_vals)) {
+      if (tid == 0) {
+        dev::mbar_arrive_expect_tx(s_mbar, (uint32_t)TILE * (CFG::KB + CFG::VB));
+        dev::tma_load_1d(s_keys, keys_in + base, (uint32_t)TILE * CFG::KB, s_mbar, pol);
+        if constexpr (HAS_V) dev::tma_load_1d(s_vals, vals_in + base, (uint32_t)TILE * CFG::VB, s_mbar, pol);
+      }
+      dev::SpinGuard guard;
+      bool ok = true;
+      while (!dev::mbar_try_wait(s_mbar, phase)) {
+        if (guard.expired(nullptr, a.spin_limit_ns)) {
+          ok = false;
+          break;
+        }
+      }
+      phase ^= 1u;
+      if (!ok) {
+        atomicOr(a.status, kStatusTmaTimeout);
+        s_misc[1] = 1;
+      }
+      __syncthreads();
+      if (s_misc[1]) break;
+    } else {
+      for (uint32_t i = tid; i < valid; i += THREADS) {
+        s_keys[i] = keys_in[base + i];
+        if constexpr (HAS_V) s_vals[i] = vals_in[base + i];
+      }
+      __syncthreads();
+    }
+
+    // ---- 2. load to registers, digit, warp ranking
+    K key[KPT];
+    uint32_t dr[KPT];  // digit | (rank within warp << 8)
+    V val[HAS_V ? KPT : 1];
+    const uint32_t wfirst = warp * (KPT * 32);
+#pragma unroll
+    for (int s = 0; s < KPT; ++s) {
+      const uint32_t idx = wfirst + s * 32 + lane;
+      key[s] = s_keys[idx];
+      dr[s] = (idx < valid) ? dev::digit_of<K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+      if constexpr (HAS_V) val[s] = s_vals[idx];
+    }
+#pragma unroll
+    for (int s = 0; s < KPT; ++s) {
+      const uint32_t r = dev::warp_rank_slot(wt, dr[s], lane, lt);
+      dr[s] |= r << 8;
+    }
+    __syncthreads();
+
+    // ---- 3. per-digit counts, aggregate publish, tile-local digit offsets
+    uint32_t cnt = 0;
+    if (tid < kRadix) {
+#pragma unroll 4
+      for (int w = 0; w < WARPS; ++w) {
+        const uint32_t c = (uint32_t)(s_wtab[w * kRadix + tid] >> 32);
+        s_wtab[w * kRadix + tid] = cnt;
+        cnt += c;
+      }
+      if (tid == a.mask) cnt -= (uint32_t)TILE - valid;
+      if (publish)
+        dev::st_relaxed(desc + (size_t)tile * kRadix + tid,
+                        DB::make(a.pass, tile == 0 ? kDescInclusive : kDescAggregate, (Off)cnt));
+    }
+    const uint32_t incl = dev::warp_inclusive_scan(cnt, lane);
+    if (lane == 31 && warp < kRadix / 32) s_misc[2 + warp] = incl;
+    __syncthreads();
+    if (tid < kRadix) {
+      uint32_t pre = 0;
+      for (uint32_t w = 0; w < warp; ++w) pre += s_misc[2 + w];
+      const uint32_t ts = pre + incl - cnt;
+      s_tstart[tid] = ts;
+#pragma unroll 4
+      for (int w = 0; w < WARPS; ++w) s_wtab[w * kRadix + tid] += ts;
+    }
+    __syncthreads();
+
+    // ---- 4. reorder in shared memory (tile sorted by digit, stable)
+#pragma unroll
+    for (int s = 0; s < KPT; ++s) {
+      const uint32_t pos = (uint32_t)wt[dr[s] & 0xffu] + (dr[s] >> 8);
+      s_keys[pos] = key[s];
+      if constexpr (HAS_V) s_vals[pos] = val[s];
+    }
+
+    // ---- 5. decoupled lookback
+    if (tid < kRadix) {
+      Off excl = 0;
+      if (tile > 0) {
+        excl = lookback_prefix<Off, kLookbackWindow>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns);
+        if (publish)
+          dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
+      }
+      s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+    }
+    __syncthreads();
+
+    // ---- 6. coalesced scatter
+    for (uint32_t j = tid; j < valid; j += THREADS) {
+      const K k = s_keys[j];
+      const Off dst = s_goff[dev::digit_of<K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+      keys_out[dst] = k;
+      if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+    }
+    dev::fence_proxy_async_smem();
+  }
+}
+
+}  // namespace cusort_b200

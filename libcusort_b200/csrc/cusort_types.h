@@ -1,0 +1,59 @@
+// cusort_types.h -- structures shared by the host dispatcher and the kernels.
+#pragma once
+
+#include <stdint.h>
+
+namespace cusort_b200 {
+
+constexpr int kRadixBits = 8;
+constexpr int kRadix = 256;
+constexpr int kMaxPasses = 8;
+
+// Device status bits (written into the control block of the temp storage).
+enum : uint32_t {
+  kStatusLookbackTimeout = 1u,  // a decoupled-lookback wait ran out of time
+  kStatusTmaTimeout = 2u,       // a bulk-copy (TMA) completion wait ran out of time
+};
+
+// Descriptor state, stored in the top two bits of each (tile, digit) word as
+// (2*pass + state) mod 4.  After pass p every word is INCLUSIVE(p), which
+// decodes as EMPTY in pass p+1, so descriptors are zeroed once per sort.
+enum : uint32_t { kDescEmpty = 0u, kDescAggregate = 1u, kDescInclusive = 2u };
+
+struct InitArgs {
+  void* ptr;      // 16-byte aligned
+  uint64_t n16;   // number of 16-byte words to zero
+};
+
+struct HistArgs {
+  const void* keys;
+  uint64_t n;
+  uint64_t tw_c, tw_f;     // twiddle constants (see dev::twiddle)
+  uint32_t begin_bit;
+  uint32_t num_passes;
+  uint32_t last_mask;      // digit mask of the last pass
+  void* g_hist;            // OffsetT[num_passes * 256]
+};
+
+struct OnesweepArgs {
+  const void* keys_in;
+  void* keys_out;
+  const void* vals_in;
+  void* vals_out;
+  uint64_t n;
+  uint64_t tw_c, tw_f;
+  uint32_t shift;          // first bit of this pass's digit
+  uint32_t mask;           // digit mask (255, or smaller on a partial last pass)
+  uint32_t pass;
+  uint32_t num_tiles;
+  void* desc;              // OffsetT[num_tiles * 256], shared by all passes
+  const void* g_hist_pass; // OffsetT[256] digit counts of this pass
+  uint32_t* tile_counter;  // dynamic tile ticket of this pass
+  uint32_t* status;        // device status word
+  uint64_t spin_limit_ns;  // bound on every wait
+  int64_t skip_tile;       // fault injection: tile that never publishes (-1 = off)
+  uint32_t tma_keys;       // keys_in/keys_out 16-byte aligned -> TMA tile loads
+  uint32_t tma_vals;
+};
+
+}  // namespace cusort_b200

@@ -1,0 +1,9 @@
+// kernels_k1.cu -- instantiates the histogram and onesweep kernels for
+// 1-byte keys (all value widths, 32- and 64-bit offsets).
+#include "cusort_instances.cuh"
+
+namespace cusort_b200 {
+bool get_kernels_k1(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram) {
+  return get_kernels_impl<1>(value_bytes, off_bytes, onesweep, histogram);
+}
+}  // namespace cusort_b200

@@ -1,0 +1,112 @@
+"""PyTorch-facing sort over the C ABI (zero-copy on CUDA tensors).
+
+``radix_sort(keys, values=None, descending=False, begin_bit=0, end_bit=None)``
+is a stable LSD radix sort of a 1-D CUDA tensor (plus an optional payload
+tensor whose leading dimension is the item count) through
+``cusort_sort_keys`` / ``cusort_sort_pairs`` of include/cusort_b200.h.
+Temporary storage is a uint8 CUDA tensor from torch's caching allocator; the
+work runs on torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _capi
+
+_DTYPE_KEY = {
+    torch.uint8: "u8", torch.int8: "i8", torch.int16: "i16", torch.int32: "i32", torch.int64: "i64",
+    torch.float32: "f32", torch.float64: "f64",
+}
+for _name, _kt in (("uint16", "u16"), ("uint32", "u32"), ("uint64", "u64")):
+    if hasattr(torch, _name):
+        _DTYPE_KEY[getattr(torch, _name)] = _kt
+
+
+def key_type_of(dtype: torch.dtype) -> str:
+    try:
+        return _DTYPE_KEY[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported key dtype {dtype}") from None
+
+
+def _value_bytes(values: torch.Tensor, n: int) -> int:
+    if values.shape[0] != n:
+        raise ValueError("values must have the item count as leading dimension")
+    if not values.is_contiguous():
+        raise ValueError("values must be contiguous")
+    vb = values.numel() * values.element_size() // max(n, 1)
+    if vb not in (1, 2, 4, 8, 16):
+        raise ValueError(f"value payload of {vb} bytes per item is not supported (1, 2, 4, 8 or 16)")
+    return vb
+
+
+def temp_storage_bytes(key_type: str, n: int, value_bytes: int = 0, begin_bit: int = 0, end_bit: int | None = None,
+                       raw: bool = True) -> int:
+    """Size query (no CUDA call), as DeviceRadixSort with d_temp_storage == nullptr."""
+    lib = _capi.load()
+    kb = _capi.KEY_BYTES[key_type]
+    end_bit = 8 * kb if end_bit is None else end_bit
+    nbytes = C.c_size_t(0)
+    kt = _capi.key_type_id(key_type)
+    if raw:
+        if value_bytes:
+            rc = lib.cusort_sort_pairs(None, C.byref(nbytes), kt, None, None, value_bytes, None, None, n,
+                                       begin_bit, end_bit, None)
+        else:
+            rc = lib.cusort_sort_keys(None, C.byref(nbytes), kt, None, None, n, begin_bit, end_bit, None)
+    else:
+        db = _capi.DoubleBufferC()
+        vdb = _capi.DoubleBufferC()
+        if value_bytes:
+            rc = lib.cusort_sort_pairs_db(None, C.byref(nbytes), kt, C.byref(db), value_bytes, C.byref(vdb), n,
+                                          begin_bit, end_bit, None)
+        else:
+            rc = lib.cusort_sort_keys_db(None, C.byref(nbytes), kt, C.byref(db), n, begin_bit, end_bit, None)
+    _capi.check(rc, "size query")
+    return nbytes.value
+
+
+def radix_sort(keys: torch.Tensor, values: torch.Tensor | None = None, *, descending: bool = False,
+               begin_bit: int = 0, end_bit: int | None = None, out_keys: torch.Tensor | None = None,
+               out_values: torch.Tensor | None = None, temp: torch.Tensor | None = None):
+    """Stable radix sort; returns (sorted_keys, sorted_values_or_None). Inputs are not modified."""
+    if not keys.is_cuda:
+        raise ValueError("keys must be a CUDA tensor (this path has no CPU implementation)")
+    if keys.dim() != 1 or not keys.is_contiguous():
+        raise ValueError("keys must be a contiguous 1-D tensor")
+    lib = _capi.load()
+    kt = key_type_of(keys.dtype)
+    n = keys.numel()
+    end_bit = 8 * keys.element_size() if end_bit is None else end_bit
+    out_keys = torch.empty_like(keys) if out_keys is None else out_keys
+    vb = 0
+    if values is not None:
+        vb = _value_bytes(values, n)
+        out_values = torch.empty_like(values) if out_values is None else out_values
+    need = temp_storage_bytes(kt, n, vb, begin_bit, end_bit, raw=True)
+    if temp is None or temp.numel() < need:
+        temp = torch.empty(max(need, 1), dtype=torch.uint8, device=keys.device)
+    nbytes = C.c_size_t(temp.numel())
+    stream = C.c_void_p(torch.cuda.current_stream(keys.device).cuda_stream)
+    kid = _capi.key_type_id(kt)
+    with torch.cuda.device(keys.device):
+        if vb:
+            fn = lib.cusort_sort_pairs_descending if descending else lib.cusort_sort_pairs
+            rc = fn(C.c_void_p(temp.data_ptr()), C.byref(nbytes), kid, C.c_void_p(keys.data_ptr()),
+                    C.c_void_p(out_keys.data_ptr()), vb, C.c_void_p(values.data_ptr()),
+                    C.c_void_p(out_values.data_ptr()), n, begin_bit, end_bit, stream)
+        else:
+            fn = lib.cusort_sort_keys_descending if descending else lib.cusort_sort_keys
+            rc = fn(C.c_void_p(temp.data_ptr()), C.byref(nbytes), kid, C.c_void_p(keys.data_ptr()),
+                    C.c_void_p(out_keys.data_ptr()), n, begin_bit, end_bit, stream)
+    _capi.check(rc, "cusort sort")
+    return out_keys, (out_values if vb else None)
+
+
+def argsort(keys: torch.Tensor, *, descending: bool = False) -> torch.Tensor:
+    """Stable argsort (int64 indices) by sorting (key, index) pairs."""
+    idx = torch.arange(keys.numel(), device=keys.device, dtype=torch.int64)
+    _, perm = radix_sort(keys, idx, descending=descending)
+    return perm

@@ -1,0 +1,200 @@
+"""GPU parity tests: libcusort_b200 (through its C ABI) against the CPU oracle,
+bit-exact, over key types, value widths, directions, bit ranges, sizes around
+tile boundaries, special floats, skewed inputs, unaligned pointers and both
+API forms; and against the reference library itself when oracle/_ref is built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from libcusort_b200 import _capi  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+from tests import datagen as D  # noqa: E402
+from tests.gpu_helpers import run_ours, run_ref, same_bits  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+
+def tile_of(kt: str, vb: int, n: int = 1 << 20) -> int:
+    lib = _capi.load()
+    tile = C.c_int(0)
+    rc = lib.cusort_query_plan(_capi.KEY_TYPES[kt], vb, n, 0, 8 * _capi.KEY_BYTES[kt], None, C.byref(tile), None,
+                               None, None)
+    assert rc == 0
+    return tile.value
+
+
+def check(kt, keys, values=None, begin=0, end=None, desc=False, api="raw", **kw):
+    ko, vo, info = run_ours(kt, keys, values, begin, end, desc, api=api, **kw)
+    ek, ev = O.oracle_sort(kt, keys, values, begin, end, desc)
+    assert same_bits(ko, ek), f"keys differ ({kt}, n={len(keys)}, bits=[{begin},{end}), desc={desc}, api={api})"
+    if values is not None:
+        assert same_bits(vo, ev), f"values differ ({kt}, n={len(keys)})"
+    return info
+
+
+# --- every key type, both directions, keys-only and pairs --------------------
+@pytest.mark.parametrize("kt", D.KEY_TYPES)
+@pytest.mark.parametrize("desc", [False, True])
+@pytest.mark.parametrize("vb", [0, 4])
+def test_key_types(kt, desc, vb):
+    n = 3 * tile_of(kt, vb) + 17
+    keys = D.uniform_bits(kt, n, seed=11 + D.KEY_TYPES.index(kt))
+    vals = D.values_for(n, vb) if vb else None
+    check(kt, keys, vals, desc=desc)
+
+
+# --- every value width ------------------------------------------------------
+@pytest.mark.parametrize("kt", ["u8", "i16", "f32", "i64", "f64"])
+@pytest.mark.parametrize("vb", [1, 2, 8, 16])
+def test_value_widths(kt, vb):
+    n = 2 * tile_of(kt, vb) + 1001
+    keys = D.uniform_bits(kt, n, seed=3)
+    check(kt, keys, D.values_for(n, vb), desc=(vb == 8))
+
+
+# --- partial bit ranges -----------------------------------------------------
+@pytest.mark.parametrize("kt,begin,end", [
+    ("u32", 0, 20), ("u32", 3, 29), ("i32", 5, 6), ("f32", 8, 16), ("f32", 0, 31), ("f32", 20, 32),
+    ("i64", 0, 64), ("i64", 17, 61), ("f64", 40, 64), ("u16", 4, 12), ("i8", 1, 8), ("u64", 63, 64),
+])
+@pytest.mark.parametrize("desc", [False, True])
+def test_bit_ranges(kt, begin, end, desc):
+    n = 50_000
+    keys = D.uniform_bits(kt, n, seed=begin * 100 + end)
+    check(kt, keys, D.values_for(n, 4), begin, end, desc)
+
+
+def test_zero_width_range_is_copy():
+    keys = D.uniform_bits("u32", 1000, seed=1)
+    vals = D.values_for(1000, 4)
+    ko, vo, _ = run_ours("u32", keys, vals, 7, 7)
+    assert same_bits(ko, keys) and same_bits(vo, vals)
+
+
+# --- sizes around tile boundaries -------------------------------------------
+@pytest.mark.parametrize("vb", [0, 4])
+def test_sizes(vb):
+    t = tile_of("u32", vb)
+    for n in [0, 1, 2, 31, 32, 33, 255, 256, 257, t - 1, t, t + 1, 2 * t, 3 * t + 17, 1 << 20]:
+        keys = D.uniform_bits("u32", n, seed=n)
+        vals = D.values_for(n, vb) if vb else None
+        check("u32", keys, vals)
+
+
+# --- distributions ------------------------------------------------------------
+@pytest.mark.parametrize("kt", ["f32", "f64"])
+@pytest.mark.parametrize("desc", [False, True])
+def test_special_floats(kt, desc):
+    n = 100_000
+    keys = D.special_floats(kt, n, seed=5, frac=0.01)
+    # a few NaN payloads and negative NaNs, denormals
+    u = keys.view(O.NP_UINT[keys.dtype.itemsize])
+    if kt == "f32":
+        u[:4] = [0x7FC00001, 0xFFC00000, 0x00000001, 0x80000001]
+    else:
+        u[:4] = [0x7FF8000000000001, 0xFFF8000000000000, 1, 0x8000000000000001]
+    check(kt, keys, D.values_for(n, 4), desc=desc)
+
+
+@pytest.mark.parametrize("kind", ["low_entropy", "all_equal", "sorted", "reversed", "zipf", "zipf_lowbits"])
+def test_distributions(kind):
+    n = 300_000
+    if kind == "low_entropy":
+        keys = D.low_entropy("i32", n, seed=3)
+    elif kind == "all_equal":
+        keys = np.full(n, 12345, dtype=np.int32)
+    elif kind == "sorted":
+        keys = np.sort(D.uniform_bits("i32", n, seed=4))
+    elif kind == "reversed":
+        keys = np.sort(D.uniform_bits("i32", n, seed=4))[::-1].copy()
+    elif kind == "zipf":
+        keys = D.zipf_table("i32", n, seed=6)
+    else:
+        keys = D.zipf_table("i32", n, seed=6, below=16)
+    check("i32", keys, D.values_for(n, 4))
+    check("i32", keys, D.values_for(n, 4), begin=0, end=20)
+
+
+# --- API forms ----------------------------------------------------------------
+@pytest.mark.parametrize("begin,end", [(0, 32), (0, 24), (0, 8), (4, 11)])
+@pytest.mark.parametrize("ksel0,vsel0", [(0, 0), (1, 0), (0, 1)])
+def test_double_buffer_selectors(begin, end, ksel0, vsel0):
+    n = 40_000
+    keys = D.uniform_bits("u32", n, seed=9)
+    vals = D.values_for(n, 8)
+    info = check("u32", keys, vals, begin, end, api="db", ksel0=ksel0, vsel0=vsel0)
+    passes = (end - begin + 7) // 8
+    assert info["ksel"] == ksel0 ^ (passes & 1)
+    assert info["vsel"] == vsel0 ^ (passes & 1)
+
+
+@pytest.mark.parametrize("kt", ["u8", "u16", "u32", "f64"])
+@pytest.mark.parametrize("offset", [1, 3])
+def test_unaligned_pointers(kt, offset):
+    n = 70_001
+    keys = D.uniform_bits(kt, n, seed=offset)
+    check(kt, keys, D.values_for(n, 2), offset_items=offset)
+    check(kt, keys, D.values_for(n, 2), offset_items=offset, api="db")
+
+
+def test_graph_mode_matches_direct():
+    n = 1 << 18
+    for seed in range(3):
+        keys = D.uniform_bits("f32", n, seed=seed)
+        vals = D.values_for(n, 4)
+        a = run_ours("f32", keys, vals, launch_mode=1)
+        b = run_ours("f32", keys, vals, launch_mode=0)
+        assert same_bits(a[0], b[0]) and same_bits(a[1], b[1])
+        ek, ev = O.oracle_sort("f32", keys, vals)
+        assert same_bits(a[0], ek) and same_bits(a[1], ev)
+
+
+def test_torch_radix_sort():
+    from libcusort_b200.torch_sort import argsort, radix_sort
+    x = torch.randn(100_003, device="cuda")
+    k, _ = radix_sort(x)
+    assert torch.equal(k, torch.sort(x, stable=True).values)
+    perm = argsort(x, descending=True)
+    assert torch.equal(perm, torch.sort(x, descending=True, stable=True).indices)
+
+
+# --- the reference library itself -------------------------------------------
+needs_ref = pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref/libcusort_ref.so not built")
+
+
+@needs_ref
+@pytest.mark.parametrize("kt", D.KEY_TYPES)
+@pytest.mark.parametrize("vb", [0, 4, 16])
+def test_reference_parity(kt, vb):
+    n = 200_000
+    keys = D.special_floats(kt, n, seed=21) if kt.startswith("f") else D.uniform_bits(kt, n, seed=21)
+    vals = D.values_for(n, vb) if vb else None
+    for desc in (False, True):
+        for api in ("raw", "db"):
+            rk, rv, rinfo = run_ref(kt, keys, vals, descending=desc, api=api)
+            ok, ov, oinfo = run_ours(kt, keys, vals, descending=desc, api=api)
+            assert same_bits(rk, ok), f"keys differ from the reference ({kt}, vb={vb}, desc={desc}, {api})"
+            if vb:
+                assert same_bits(rv, ov)
+            if api == "db":
+                assert rinfo["ksel"] == oinfo["ksel"] and rinfo["vsel"] == oinfo["vsel"]
+
+
+@needs_ref
+@pytest.mark.parametrize("kt,begin,end", [("u32", 0, 20), ("f32", 3, 29), ("f64", 11, 50), ("i16", 2, 9)])
+def test_reference_parity_bit_ranges(kt, begin, end):
+    n = 123_457
+    keys = D.uniform_bits(kt, n, seed=begin + end)
+    vals = D.values_for(n, 4)
+    rk, rv, _ = run_ref(kt, keys, vals, begin, end, True)
+    ok, ov, _ = run_ours(kt, keys, vals, begin, end, True)
+    assert same_bits(rk, ok) and same_bits(rv, ov)
