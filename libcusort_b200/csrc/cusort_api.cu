@@ -281,7 +281,7 @@ static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers
     const uint64_t want = (vec + p.hist.tile - 1) / p.hist.tile;
     l.grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ_h, want));
     l.threads = p.hist.threads;
-    l.smem = 0;
+    l.smem = p.hist.smem;
     l.pdl = true;
     l.kind = 1;
     HistArgs& h = l.args.hist;

@@ -22,7 +22,7 @@ struct TileShape {
   static constexpr int MINB = 2;
 };
 
-constexpr int kHistThreads = 512;
+constexpr int kHistThreads = 1024;
 constexpr int kHistUnroll = 4;
 
 template <int KB, int VB, typename Off>
@@ -40,7 +40,7 @@ inline void fill_histogram(KernelInfo* h) {
   h->func = reinterpret_cast<const void*>(&histogram_kernel<KB, Off, kHistThreads, kHistUnroll>);
   h->threads = kHistThreads;
   h->tile = kHistThreads * kHistUnroll;
-  h->smem = 0;
+  h->smem = HistShape<KB>::SMEM;
 }
 
 template <int KB, typename Off>

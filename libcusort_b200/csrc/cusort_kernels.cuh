@@ -22,20 +22,33 @@ __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + 
 // ---------------------------------------------------------------------------
 // histogram: digit counts of every pass from ONE read of the keys.
 // 16-byte streaming loads (ld.global.nc.L1::no_allocate.v4), UNROLL vectors in
-// flight per thread, per-CTA shared-memory counters, one global atomic per
-// (pass, digit) per CTA.  The global atomics wait for the init kernel (PDL);
-// the key reads and shared-memory counting overlap it.
+// flight per thread, one persistent CTA per SM.  Shared-memory counters are
+// replicated R times and laid out [pass][digit][replica] so that lane l always
+// increments replica l % R: with R = 32 every lane of a warp hits its own bank
+// and the P shared atomics per key are conflict-free (a single 256-bin table
+// costs ~3.5 wavefronts per warp atomic for random digits).  The replicas are
+// summed once per CTA into one global atomic per (pass, digit).  The global
+// atomics wait for the init kernel (PDL); reads and counting overlap it.
 // ---------------------------------------------------------------------------
+template <int KB>
+struct HistShape {
+  static constexpr int MAXP = KB;  // 8-bit digits: at most one pass per key byte
+  static constexpr int R = (KB == 8) ? 16 : 32;
+  static constexpr size_t SMEM = (size_t)MAXP * kRadix * R * 4;
+};
+
 template <int KB, typename Off, int THREADS, int UNROLL>
-__global__ void __launch_bounds__(THREADS) histogram_kernel(const HistArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a) {
   using K = typename dev::UIntOf<KB>::T;
-  constexpr int MAXP = KB;            // 8-bit digits: at most one pass per key byte
-  constexpr int PER = 16 / KB;        // keys per 16-byte vector
-  __shared__ uint32_t s_hist[MAXP * kRadix];
+  using HS = HistShape<KB>;
+  constexpr int MAXP = HS::MAXP, R = HS::R;
+  constexpr int PER = 16 / KB;  // keys per 16-byte vector
+  extern __shared__ __align__(16) uint32_t s_hist[];
 
   dev::pdl_launch_dependents();
   const uint32_t tid = threadIdx.x;
-  for (uint32_t i = tid; i < MAXP * kRadix; i += THREADS) s_hist[i] = 0;
+  const uint32_t rep = tid % R;
+  for (uint32_t i = tid; i < MAXP * kRadix * R; i += THREADS) s_hist[i] = 0;
   __syncthreads();
 
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
@@ -47,7 +60,7 @@ __global__ void __launch_bounds__(THREADS) histogram_kernel(const HistArgs a) {
       if (p < (int)P) {
         const uint32_t m = (p + 1 == (int)P) ? a.last_mask : 0xffu;
         const uint32_t d = (uint32_t)(t >> (a.begin_bit + 8 * p)) & m;
-        atomicAdd(&s_hist[p * kRadix + d], 1u);
+        atomicAdd(&s_hist[(p * kRadix + d) * R + rep], 1u);
       }
     }
   };
@@ -88,7 +101,9 @@ __global__ void __launch_bounds__(THREADS) histogram_kernel(const HistArgs a) {
   dev::pdl_wait();  // g_hist zeroed by init_kernel
   Off* g = static_cast<Off*>(a.g_hist);
   for (uint32_t i = tid; i < P * kRadix; i += THREADS) {
-    const uint32_t c = s_hist[i];
+    uint32_t c = 0;
+#pragma unroll 8
+    for (int r = 0; r < R; ++r) c += s_hist[i * R + ((r + i) % R)];  // rotated: conflict-free
     if (c) atomicAdd(g + i, (Off)c);
   }
 }
@@ -112,16 +127,136 @@ __global__ void __launch_bounds__(THREADS) histogram_kernel(const HistArgs a) {
 // Out-of-range slots of the last tile take the top digit and are never
 // written (their sorted positions are >= the tile's valid count).
 // ---------------------------------------------------------------------------
+// Warp ranking variants (see WarpCounters): 0 = shared-memory match,
+// 1 = ballot match with 16-bit per-warp counters, 2 = hybrid (default; the
+// fastest of the three on B200 for every key/value width measured).
+#ifndef CUSORT_RANK_MODE
+#define CUSORT_RANK_MODE 2
+#endif
+
+template <int MODE>
+struct WarpCounters;
+
+// Shared-memory match (dev::warp_rank_slot): one 64-bit [count | lane mask]
+// word per (warp, digit).
+template <>
+struct WarpCounters<0> {
+  using Word = unsigned long long;
+  static constexpr size_t BYTES_PER_WARP = kRadix * 8;
+  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
+    Word* w = reinterpret_cast<Word*>(tab) + warp * kRadix;
+#pragma unroll
+    for (int i = 0; i < kRadix / 32; ++i) w[lane + 32 * i] = 0ull;
+  }
+  __device__ __forceinline__ static uint32_t rank(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                  uint32_t lt) {
+    return dev::warp_rank_slot(reinterpret_cast<Word*>(tab) + warp * kRadix, d, lane, lt);
+  }
+  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return (uint32_t)(reinterpret_cast<const Word*>(tab)[w * kRadix + t] >> 32);
+  }
+  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return (uint32_t)reinterpret_cast<const Word*>(tab)[w * kRadix + t];
+  }
+  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
+    reinterpret_cast<Word*>(tab)[w * kRadix + t] = v;
+  }
+};
+
+// Ballot match (8 vote.ballot per slot, no shared-memory traffic) plus one
+// 16-bit counter per (warp, digit): the highest peer lane adds the group size
+// with a 32-bit shared atomic on the word holding two counters and shuffles
+// the previous count to its peers.
+template <>
+struct WarpCounters<1> {
+  static constexpr size_t BYTES_PER_WARP = kRadix * 2;
+  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(tab) + warp * (kRadix / 2);
+#pragma unroll
+    for (int i = 0; i < kRadix / 64; ++i) w[lane + 32 * i] = 0u;
+  }
+  __device__ __forceinline__ static uint32_t rank(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                  uint32_t lt) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(tab) + warp * (kRadix / 2);
+    const uint32_t peers = dev::match_digit_ballot<8>(d);
+    const uint32_t below = __popc(peers & lt);
+    const uint32_t leader = 31u - __clz(peers);
+    const uint32_t sh = (d & 1u) << 4;
+    uint32_t old = 0;
+    if (lane == leader) old = atomicAdd(w + (d >> 1), (below + 1u) << sh);
+    old = __shfl_sync(0xffffffffu, old, leader);
+    return ((old >> sh) & 0xffffu) + below;
+  }
+  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint16_t*>(tab)[w * kRadix + t];
+  }
+  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint16_t*>(tab)[w * kRadix + t];
+  }
+  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
+    reinterpret_cast<uint16_t*>(tab)[w * kRadix + t] = (uint16_t)v;
+  }
+};
+
+// Hybrid: the low 2 digit bits by ballot, the high 6 bits by a shared-memory
+// match on a 64-word per-warp table (two bank rows, so far fewer bank
+// conflicts than a 256-entry table), then the 16-bit counters of mode 1.
+template <>
+struct WarpCounters<2> {
+  static constexpr size_t MASK_WORDS = 64;
+  static constexpr size_t BYTES_PER_WARP = kRadix * 2 + MASK_WORDS * 4;
+  __device__ __forceinline__ static uint32_t* masks(uint8_t* tab, uint32_t warp) {
+    return reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP + kRadix * 2);
+  }
+  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+#pragma unroll
+    for (int i = 0; i < (int)(BYTES_PER_WARP / 4 / 32); ++i) w[lane + 32 * i] = 0u;
+  }
+  __device__ __forceinline__ static uint32_t rank(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                  uint32_t lt) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    uint32_t* msk = masks(tab, warp);
+    const uint32_t hi = d >> 2;
+    atomicOr(msk + hi, 1u << lane);
+    const uint32_t pl = dev::match_digit_ballot<2>(d);
+    __syncwarp();
+    const uint32_t ph = msk[hi];
+    __syncwarp();
+    if ((ph >> lane) == 1u) msk[hi] = 0u;
+    const uint32_t peers = pl & ph;
+    const uint32_t below = __popc(peers & lt);
+    const uint32_t leader = 31u - __clz(peers);
+    const uint32_t sh = (d & 1u) << 4;
+    uint32_t old = 0;
+    if (lane == leader) old = atomicAdd(cnt + (d >> 1), (below + 1u) << sh);
+    old = __shfl_sync(0xffffffffu, old, leader);
+    __syncwarp();
+    return ((old >> sh) & 0xffffu) + below;
+  }
+  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint16_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint16_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
+    reinterpret_cast<uint16_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = (uint16_t)v;
+  }
+};
+
 template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_>
 struct OnesweepCfg {
   static constexpr int KB = KB_, VB = VB_, THREADS = THREADS_, KPT = KPT_, MINB = MINB_;
+  static constexpr int RANK_MODE = CUSORT_RANK_MODE;
+  using WC = WarpCounters<RANK_MODE>;
   using Off = Off_;
   static constexpr int WARPS = THREADS / 32;
   static constexpr int TILE = THREADS * KPT;
   static constexpr size_t OFF_KEYS = 0;
   static constexpr size_t OFF_VALS = align_up(OFF_KEYS + (size_t)TILE * KB, 128);
   static constexpr size_t OFF_WTAB = align_up(OFF_VALS + (size_t)TILE * VB, 128);
-  static constexpr size_t OFF_TSTART = OFF_WTAB + (size_t)WARPS * kRadix * 8;
+  static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
   static constexpr size_t OFF_GBASE = OFF_TSTART + kRadix * 4;
   static constexpr size_t OFF_GOFF = OFF_GBASE + kRadix * sizeof(Off);
   static constexpr size_t OFF_MISC = OFF_GOFF + kRadix * sizeof(Off);
@@ -130,6 +265,7 @@ struct OnesweepCfg {
   static_assert(THREADS >= kRadix && THREADS % 32 == 0, "need >= 256 threads");
   static_assert(TILE * (KB + VB) < (1 << 20), "mbarrier tx-count limit");
   static_assert(32 * KPT < (1 << 24), "rank packing");
+  static_assert(TILE <= 65536, "16-bit tile positions");
 };
 
 constexpr int kLookbackWindow = 8;
@@ -199,7 +335,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   extern __shared__ __align__(128) uint8_t smem[];
   K* s_keys = reinterpret_cast<K*>(smem + CFG::OFF_KEYS);
   V* s_vals = reinterpret_cast<V*>(smem + CFG::OFF_VALS);
-  unsigned long long* s_wtab = reinterpret_cast<unsigned long long*>(smem + CFG::OFF_WTAB);
+  uint8_t* s_wtab = smem + CFG::OFF_WTAB;
+  using WC = typename CFG::WC;
   uint32_t* s_tstart = reinterpret_cast<uint32_t*>(smem + CFG::OFF_TSTART);
   Off* s_gbase = reinterpret_cast<Off*>(smem + CFG::OFF_GBASE);
   Off* s_goff = reinterpret_cast<Off*>(smem + CFG::OFF_GOFF);
@@ -225,11 +362,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   // Global exclusive offset of every digit for this pass (from the upfront
   // histogram), computed once per CTA.
   {
-    uint32_t c = 0;
-    if (tid < kRadix) c = (uint32_t)static_cast<const Off*>(a.g_hist_pass)[tid];
-    // 64-bit totals can exceed 32 bits only for n > 2^32; scan in Off.
     Off cv = (tid < kRadix) ? static_cast<const Off*>(a.g_hist_pass)[tid] : Off(0);
-    (void)c;
     Off incl = cv;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -249,12 +382,10 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   const uint64_t pol = dev::l2_policy_evict_first();
   uint32_t phase = 0;
   const uint32_t lt = dev::lanemask_lt();
-  unsigned long long* wt = s_wtab + warp * kRadix;
 
   for (;;) {
     if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
-#pragma unroll
-    for (int i = 0; i < kRadix / 32; ++i) wt[lane + 32 * i] = 0ull;
+    WC::zero(s_wtab, warp, lane);
     __syncthreads();
     const uint32_t tile = s_misc[0];
     if (tile >= a.num_tiles) break;
@@ -306,7 +437,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
 #pragma unroll
     for (int s = 0; s < KPT; ++s) {
-      const uint32_t r = dev::warp_rank_slot(wt, dr[s], lane, lt);
+      const uint32_t r = WC::rank(s_wtab, warp, dr[s], lane, lt);
       dr[s] |= r << 8;
     }
     __syncthreads();
@@ -316,8 +447,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     if (tid < kRadix) {
 #pragma unroll 4
       for (int w = 0; w < WARPS; ++w) {
-        const uint32_t c = (uint32_t)(s_wtab[w * kRadix + tid] >> 32);
-        s_wtab[w * kRadix + tid] = cnt;
+        const uint32_t c = WC::count(s_wtab, w, tid);
+        WC::put(s_wtab, w, tid, cnt);
         cnt += c;
       }
       if (tid == a.mask) cnt -= (uint32_t)TILE - valid;
@@ -334,14 +465,14 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       const uint32_t ts = pre + incl - cnt;
       s_tstart[tid] = ts;
 #pragma unroll 4
-      for (int w = 0; w < WARPS; ++w) s_wtab[w * kRadix + tid] += ts;
+      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
     }
     __syncthreads();
 
     // ---- 4. reorder in shared memory (tile sorted by digit, stable)
 #pragma unroll
     for (int s = 0; s < KPT; ++s) {
-      const uint32_t pos = (uint32_t)wt[dr[s] & 0xffu] + (dr[s] >> 8);
+      const uint32_t pos = WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8);
       s_keys[pos] = key[s];
       if constexpr (HAS_V) s_vals[pos] = val[s];
     }
