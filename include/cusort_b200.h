@@ -115,6 +115,36 @@ cudaError_t cusort_sort_pairs_descending(void* d_temp_storage, size_t* temp_stor
                                          size_t value_bytes, const void* d_values_in, void* d_values_out,
                                          int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
 
+/* ---- sorting without any device allocation ----------------------------
+ * No counterpart in the reference (which always takes temp storage from the
+ * caller).  For callers that cannot allocate device memory when they need to
+ * sort: a custom allocator or memory-pool hook sorting its own bookkeeping
+ * (allocating from inside it would re-enter the allocator), a plugin in a host
+ * process that has reserved all device memory up front, or a latency-bound
+ * loop where cudaMalloc would synchronise the device.
+ *
+ * Sorts a DoubleBuffer of keys (value_bytes == 0, d_values may be NULL) or of
+ * key/value pairs (value_bytes 1, 2, 4, 8 or 16), ascending or descending
+ * (`descending` != 0), exactly like cusort_sort_keys_db / cusort_sort_pairs_db
+ * (same results, same selector updates), but its temp storage is one fixed
+ * array of CUSORT_NOALLOC_SCRATCH_BYTES that the library keeps in device
+ * memory.  It calls no cudaMalloc, cudaFree or allocating library routine.
+ *   - Limit: a call whose temp storage would exceed the array returns
+ *     cudaErrorInvalidValue and does nothing.  The temp storage is about
+ *     1 KiB per 8192-item tile plus 2 KiB (e.g. 2^25 32-bit keys fit in 4 MiB).
+ *   - The array occupies CUSORT_NOALLOC_SCRATCH_BYTES on every GPU where this
+ *     entry point has run, until the process exits.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the one array and it keeps the last call's contents:
+ *     calls whose GPU work can overlap (other streams, other host threads on
+ *     the same device) race on it and corrupt each other's results, so
+ *     serialise them (e.g. one stream). */
+#define CUSORT_NOALLOC_SCRATCH_BYTES (4u << 20)
+cudaError_t cusort_sort_db_noalloc(cusort_key_type key_type, cusort_double_buffer* d_keys, size_t value_bytes,
+                                   cusort_double_buffer* d_values, int64_t num_items, int begin_bit, int end_bit,
+                                   int descending, cudaStream_t stream);
+
 /* ---- library state, status and diagnostics (no reference counterpart;
  *      the reference has compile-time macros only, libcusort.cuh:119-148) -- */
 

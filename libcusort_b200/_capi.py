@@ -41,6 +41,7 @@ SIGNATURES = {
     "cusort_sort_keys_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
+    "cusort_sort_db_noalloc": (_i, [_i, _P_DB, _sz, _P_DB, _i64, _i, _i, _i, _vp]),
     "cusort_version": (C.c_char_p, []),
     "cusort_set_launch_mode": (_i, [_i]),
     "cusort_read_device_status": (_i, [_vp, C.POINTER(_u32), _vp]),

@@ -432,6 +432,7 @@ struct SortCall {
   int64_t n;
   int begin, end;
   cudaStream_t stream;
+  bool force_direct;  // never build/replay a graph (no-allocation entry point)
 };
 
 static cudaError_t sort_impl(const SortCall& c) {
@@ -495,7 +496,7 @@ static cudaError_t sort_impl(const SortCall& c) {
 
   std::vector<Launch> ls;
   CUSORT_TRY(build_launches(p, c.d_temp, b, &ls));
-  if (g_ts.launch_mode == 1 && !g_ts.timing)
+  if (g_ts.launch_mode == 1 && !g_ts.timing && !c.force_direct)
     CUSORT_TRY(launch_graph(ls, c.stream));
   else
     CUSORT_TRY(launch_direct(ls, c.stream));
@@ -505,6 +506,36 @@ static cudaError_t sort_impl(const SortCall& c) {
     if (c.vb) c.vdb->selector ^= (int)(p.passes & 1u);
   }
   return cudaSuccess;
+}
+
+// DoubleBuffer sort whose temp storage is a caller-provided scratch region
+// of `scratch_bytes` (used by the no-allocation entry point): rejects calls
+// whose temp storage would not fit, and always launches directly.
+cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int kt, size_t vb, bool desc,
+                               cusort_double_buffer* k, cusort_double_buffer* v, int64_t n, int begin, int end,
+                               cudaStream_t stream) {
+  SortCall c = {};
+  c.temp_bytes = nullptr;
+  c.kt = kt;
+  c.vb = vb;
+  c.desc = desc;
+  c.raw = false;
+  c.kdb = k;
+  c.vdb = v;
+  c.n = n;
+  c.begin = begin;
+  c.end = end;
+  c.stream = stream;
+  c.force_direct = true;
+  size_t need = 0;
+  c.d_temp = nullptr;
+  c.temp_bytes = &need;
+  CUSORT_TRY(sort_impl(c));
+  if (need > scratch_bytes) return cudaErrorInvalidValue;
+  size_t have = scratch_bytes;
+  c.d_temp = scratch;
+  c.temp_bytes = &have;
+  return sort_impl(c);
 }
 
 }  // namespace cusort_b200

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+struct cusort_double_buffer;
+
 namespace cusort_b200 {
 
 struct KernelInfo {
@@ -21,5 +23,10 @@ bool get_kernels_k2(int value_bytes, int off_bytes, KernelInfo* onesweep, Kernel
 bool get_kernels_k4(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram);
 bool get_kernels_k8(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram);
 const void* get_init_kernel();
+
+// DoubleBuffer sort with `scratch` as its temp storage (cusort_api.cu).
+cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type, size_t value_bytes, bool descending,
+                               struct cusort_double_buffer* keys, struct cusort_double_buffer* values,
+                               int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
 
 }  // namespace cusort_b200
