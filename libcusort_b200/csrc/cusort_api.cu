@@ -154,11 +154,12 @@ static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int e
   p->last_mask = (1u << (nbits - (p->passes - 1) * kRadixBits)) - 1u;
   twiddle_constants(kt, p->kb, desc, &p->tw_c, &p->tw_f);
   bool ok = false;
+  const bool fk = (kt == CUSORT_KEY_F32 || kt == CUSORT_KEY_F64);
   switch (p->kb) {
-    case 1: ok = get_kernels_k1(p->vb, p->offb, &p->os, &p->hist); break;
-    case 2: ok = get_kernels_k2(p->vb, p->offb, &p->os, &p->hist); break;
-    case 4: ok = get_kernels_k4(p->vb, p->offb, &p->os, &p->hist); break;
-    case 8: ok = get_kernels_k8(p->vb, p->offb, &p->os, &p->hist); break;
+    case 1: ok = get_kernels_k1(p->vb, p->offb, fk, &p->os, &p->hist); break;
+    case 2: ok = get_kernels_k2(p->vb, p->offb, fk, &p->os, &p->hist); break;
+    case 4: ok = get_kernels_k4(p->vb, p->offb, fk, &p->os, &p->hist); break;
+    case 8: ok = get_kernels_k8(p->vb, p->offb, fk, &p->os, &p->hist); break;
     default: ok = false;
   }
   if (!ok) return false;

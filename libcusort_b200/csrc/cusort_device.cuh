@@ -49,6 +49,45 @@ __device__ __forceinline__ uint32_t digit_of(U x, U c, U f, uint32_t shift, uint
   return (uint32_t)(twiddle<U>(x, c, f) >> shift) & mask;
 }
 
+// Twiddle of one key type class: integer keys only need the xor constant
+// (F == 0), floating-point keys the sign-dependent term as well.
+template <bool FLOAT_KEY, typename U>
+__device__ __forceinline__ U twiddle_k(U x, U c, U f) {
+  if constexpr (FLOAT_KEY) return twiddle<U>(x, c, f);
+  else return (U)(x ^ c);
+}
+template <bool FLOAT_KEY, typename U>
+__device__ __forceinline__ uint32_t digit_k(U x, U c, U f, uint32_t shift, uint32_t mask) {
+  return (uint32_t)(twiddle_k<FLOAT_KEY, U>(x, c, f) >> shift) & mask;
+}
+
+// Streaming (evict-first) global loads of one element.
+__device__ __forceinline__ uint8_t ld_cs(const uint8_t* p) {
+  uint16_t v;
+  asm volatile("ld.global.cs.u8 %0, [%1];" : "=h"(v) : "l"(p));
+  return (uint8_t)v;
+}
+__device__ __forceinline__ uint16_t ld_cs(const uint16_t* p) {
+  uint16_t v;
+  asm volatile("ld.global.cs.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_cs(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.cs.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_cs(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cs.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_cs(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // PTX helpers
 // ---------------------------------------------------------------------------
@@ -201,6 +240,17 @@ __device__ __forceinline__ uint32_t match_digit_ballot(uint32_t d) {
     m &= ~(v ^ (0u - bit));
   }
   return m;
+}
+
+// Predicated shared-memory atomic add (no branch): when `pred` is false the
+// instruction is skipped and the previous content of `old` is returned.
+__device__ __forceinline__ uint32_t atom_add_shared_if(uint32_t pred, uint32_t* addr, uint32_t v, uint32_t old) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %1, 0;\n @p atom.shared.add.u32 %0, [%2], %3;\n}\n"
+      : "+r"(old)
+      : "r"(pred), "r"(smem_u32(addr)), "r"(v)
+      : "memory");
+  return old;
 }
 
 // Inclusive warp scan (shfl_up) of 32-bit values.

@@ -17,11 +17,12 @@ struct KernelInfo {
   size_t smem = 0;             // dynamic shared memory bytes
 };
 
-// One entry per key width; value bytes in {0,1,2,4,8,16}, off_bytes in {4,8}.
-bool get_kernels_k1(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram);
-bool get_kernels_k2(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram);
-bool get_kernels_k4(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram);
-bool get_kernels_k8(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram);
+// One entry per key width; value bytes in {0,1,2,4,8,16}, off_bytes in {4,8};
+// float_key selects the floating-point twiddle (4- and 8-byte keys only).
+bool get_kernels_k1(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
+bool get_kernels_k2(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
+bool get_kernels_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
+bool get_kernels_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 const void* get_init_kernel();
 
 // DoubleBuffer sort with `scratch` as its temp storage (cusort_api.cu).

@@ -14,59 +14,94 @@
 
 namespace cusort_b200 {
 
+#ifndef CUSORT_OS_THREADS
+#define CUSORT_OS_THREADS 512
+#endif
+#ifndef CUSORT_OS_MINB
+#define CUSORT_OS_MINB 2
+#endif
+// Items per thread by bytes per item (key + value); overridable for tuning.
+#ifndef CUSORT_OS_KPT_LE4
+#define CUSORT_OS_KPT_LE4 16
+#endif
+#ifndef CUSORT_OS_KPT_LE8
+#define CUSORT_OS_KPT_LE8 16
+#endif
+#ifndef CUSORT_OS_KPT_LE16
+#define CUSORT_OS_KPT_LE16 12
+#endif
+#ifndef CUSORT_OS_KPT_GT16
+#define CUSORT_OS_KPT_GT16 8
+#endif
+
 template <int KB, int VB>
 struct TileShape {
-  static constexpr int THREADS = 512;
+  static constexpr int THREADS = CUSORT_OS_THREADS;
   static constexpr int BYTES = KB + VB;
-  static constexpr int KPT = (KB == 8 && VB >= 8) ? 8 : (BYTES > 16) ? 8 : (BYTES > 8) ? 12 : 16;
-  static constexpr int MINB = 2;
+  static constexpr int KPT = (KB == 8 && VB >= 8) ? CUSORT_OS_KPT_GT16
+                             : (BYTES > 16)       ? CUSORT_OS_KPT_GT16
+                             : (BYTES > 8)        ? CUSORT_OS_KPT_LE16
+                             : (BYTES > 4)        ? CUSORT_OS_KPT_LE8
+                                                  : CUSORT_OS_KPT_LE4;
+  static constexpr int MINB = CUSORT_OS_MINB;
 };
 
 constexpr int kHistThreads = 1024;
 constexpr int kHistUnroll = 4;
 
-template <int KB, int VB, typename Off>
+template <int KB, int VB, typename Off, bool FK>
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB>;
-  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB>;
+  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK>;
   os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;
   os->tile = CFG::TILE;
   os->smem = CFG::SMEM_BYTES;
 }
 
-template <int KB, typename Off>
+template <int KB, typename Off, bool FK>
 inline void fill_histogram(KernelInfo* h) {
-  h->func = reinterpret_cast<const void*>(&histogram_kernel<KB, Off, kHistThreads, kHistUnroll>);
+  h->func = reinterpret_cast<const void*>(&histogram_kernel<KB, Off, kHistThreads, kHistUnroll, FK>);
   h->threads = kHistThreads;
   h->tile = kHistThreads * kHistUnroll;
   h->smem = HistShape<KB>::SMEM;
 }
 
-template <int KB, typename Off>
+template <int KB, typename Off, bool FK>
 inline bool fill_for_value(int vb, KernelInfo* os) {
   switch (vb) {
-    case 0: fill_onesweep<KB, 0, Off>(os); return true;
-    case 1: fill_onesweep<KB, 1, Off>(os); return true;
-    case 2: fill_onesweep<KB, 2, Off>(os); return true;
-    case 4: fill_onesweep<KB, 4, Off>(os); return true;
-    case 8: fill_onesweep<KB, 8, Off>(os); return true;
-    case 16: fill_onesweep<KB, 16, Off>(os); return true;
+    case 0: fill_onesweep<KB, 0, Off, FK>(os); return true;
+    case 1: fill_onesweep<KB, 1, Off, FK>(os); return true;
+    case 2: fill_onesweep<KB, 2, Off, FK>(os); return true;
+    case 4: fill_onesweep<KB, 4, Off, FK>(os); return true;
+    case 8: fill_onesweep<KB, 8, Off, FK>(os); return true;
+    case 16: fill_onesweep<KB, 16, Off, FK>(os); return true;
     default: return false;
   }
 }
 
-template <int KB>
-inline bool get_kernels_impl(int vb, int offb, KernelInfo* os, KernelInfo* h) {
+// Floating-point keys exist only at 4 and 8 bytes.
+template <int KB, bool FK>
+inline bool get_kernels_fk(int vb, int offb, KernelInfo* os, KernelInfo* h) {
   if (offb == 4) {
-    fill_histogram<KB, unsigned int>(h);
-    return fill_for_value<KB, unsigned int>(vb, os);
+    fill_histogram<KB, unsigned int, FK>(h);
+    return fill_for_value<KB, unsigned int, FK>(vb, os);
   }
   if (offb == 8) {
-    fill_histogram<KB, unsigned long long>(h);
-    return fill_for_value<KB, unsigned long long>(vb, os);
+    fill_histogram<KB, unsigned long long, FK>(h);
+    return fill_for_value<KB, unsigned long long, FK>(vb, os);
   }
   return false;
+}
+
+template <int KB>
+inline bool get_kernels_impl(int vb, int offb, bool float_key, KernelInfo* os, KernelInfo* h) {
+  if constexpr (KB == 4 || KB == 8) {
+    if (float_key) return get_kernels_fk<KB, true>(vb, offb, os, h);
+  } else {
+    if (float_key) return false;
+  }
+  return get_kernels_fk<KB, false>(vb, offb, os, h);
 }
 
 }  // namespace cusort_b200

@@ -13,6 +13,8 @@
 // are re-designed for sm_100a (see the per-kernel comments).
 #pragma once
 
+#include <type_traits>
+
 #include "cusort_device.cuh"
 
 namespace cusort_b200 {
@@ -37,7 +39,7 @@ struct HistShape {
   static constexpr size_t SMEM = (size_t)MAXP * kRadix * R * 4;
 };
 
-template <int KB, typename Off, int THREADS, int UNROLL>
+template <int KB, typename Off, int THREADS, int UNROLL, bool FLOAT_KEY>
 __global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a) {
   using K = typename dev::UIntOf<KB>::T;
   using HS = HistShape<KB>;
@@ -53,14 +55,15 @@ __global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a)
 
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
   const uint32_t P = a.num_passes;
+  uint32_t* my_hist = s_hist + rep;
   auto count = [&](K k) {
-    const K t = dev::twiddle<K>(k, tc, tf);
+    const K t = dev::twiddle_k<FLOAT_KEY, K>(k, tc, tf);
 #pragma unroll
     for (int p = 0; p < MAXP; ++p) {
       if (p < (int)P) {
         const uint32_t m = (p + 1 == (int)P) ? a.last_mask : 0xffu;
         const uint32_t d = (uint32_t)(t >> (a.begin_bit + 8 * p)) & m;
-        atomicAdd(&s_hist[(p * kRadix + d) * R + rep], 1u);
+        atomicAdd(my_hist + (p * kRadix + d) * R, 1u);
       }
     }
   };
@@ -128,10 +131,11 @@ __global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a)
 // written (their sorted positions are >= the tile's valid count).
 // ---------------------------------------------------------------------------
 // Warp ranking variants (see WarpCounters): 0 = shared-memory match,
-// 1 = ballot match with 16-bit per-warp counters, 2 = hybrid (default; the
-// fastest of the three on B200 for every key/value width measured).
+// 1 = ballot match with 16-bit per-warp counters, 2 = hybrid ballot/shared
+// match, 3 = hybrid with rotating tables and no branches, 4 = mode 3 after a
+// counting pre-pass (early aggregate publish, ranks are final positions).
 #ifndef CUSORT_RANK_MODE
-#define CUSORT_RANK_MODE 2
+#define CUSORT_RANK_MODE -1  // per key/value width, see OnesweepCfg::RANK_MODE
 #endif
 
 template <int MODE>
@@ -245,23 +249,133 @@ struct WarpCounters<2> {
   }
 };
 
-template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_>
+// Mode 3: the hybrid of mode 2 with three mask tables used in rotation, so a
+// slot clears the table of the slot before it and one warp barrier per slot
+// suffices; the clears are unconditional stores and the counter update is a
+// predicated atomic (no branches).  rank() takes the slot index and carries the
+// previous slot's table word index per lane.
+template <>
+struct WarpCounters<3> {
+  static constexpr int NT = 3;
+  static constexpr size_t MASK_WORDS = 64;
+  static constexpr size_t BYTES_PER_WARP = kRadix * 2 + NT * MASK_WORDS * 4;
+  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+#pragma unroll
+    for (int i = 0; i < (int)(BYTES_PER_WARP / 4 / 32); ++i) w[lane + 32 * i] = 0u;
+  }
+  template <int S>
+  __device__ __forceinline__ static uint32_t rank_slot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                       uint32_t lt, uint32_t& prev_word) {
+    uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    uint32_t* cnt = base;
+    uint32_t* msk = base + kRadix / 2;
+    const uint32_t word = (uint32_t)(S % NT) * MASK_WORDS + (d >> 2);
+    atomicOr(msk + word, 1u << lane);
+    const uint32_t pl = dev::match_digit_ballot<2>(d);
+    __syncwarp();
+    const uint32_t ph = msk[word];
+    if (S > 0) msk[prev_word] = 0u;  // previous slot's table: read by all lanes before the barrier above
+    prev_word = word;
+    const uint32_t peers = pl & ph;
+    const uint32_t below = __popc(peers & lt);
+    const uint32_t leader = 31u - __clz(peers);
+    const uint32_t sh = (d & 1u) << 4;
+    uint32_t old = dev::atom_add_shared_if(lane == leader, cnt + (d >> 1), (below + 1u) << sh, 0u);
+    old = __shfl_sync(0xffffffffu, old, leader);
+    return ((old >> sh) & 0xffffu) + below;
+  }
+  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint16_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint16_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
+    reinterpret_cast<uint16_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = (uint16_t)v;
+  }
+};
+
+// Mode 4: per-warp digit counts are taken first (one shared atomic per key on
+// the 16-bit counters), so the tile's aggregate can be published before the
+// expensive ranking; the counters are then turned into each warp's final tile
+// positions and the ranking atomics of mode 3 return positions directly.
+template <>
+struct WarpCounters<4> : WarpCounters<3> {
+  __device__ __forceinline__ static void count_key(uint8_t* tab, uint32_t warp, uint32_t d) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    atomicAdd(cnt + (d >> 1), 1u << ((d & 1u) << 4));
+  }
+};
+
+template <int S, int N, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (S < N) {
+    f(std::integral_constant<int, S>{});
+    static_for<S + 1, N>(f);
+  }
+}
+
+template <int MODE, int S>
+struct RankStep {
+  __device__ __forceinline__ static uint32_t run(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane, uint32_t lt,
+                                                 uint32_t& prev) {
+    if constexpr (MODE == 3) return WarpCounters<3>::rank_slot<S>(tab, warp, d, lane, lt, prev);
+    else return WarpCounters<MODE>::rank(tab, warp, d, lane, lt);
+  }
+};
+
+// Unrolled slot loop with the slot index as a compile-time constant.
+template <int MODE, int S, int KPT>
+struct RankSlots {
+  __device__ __forceinline__ static void run(uint8_t* tab, uint32_t warp, uint32_t* dr, uint32_t lane, uint32_t lt,
+                                             uint32_t& prev) {
+    if constexpr (S < KPT) {
+      const uint32_t r = RankStep<MODE, S>::run(tab, warp, dr[S], lane, lt, prev);
+      dr[S] |= r << 8;
+      RankSlots<MODE, S + 1, KPT>::run(tab, warp, dr, lane, lt, prev);
+    }
+  }
+};
+
+// Tile prefetch: 1 = take the next tile's ticket one tile ahead and TMA-load
+// it into a second buffer while the current tile is processed.  Off by
+// default: on B200 the early tickets delay those tiles' descriptors and the
+// longer lookback waits cost more than the hidden load latency (u32 keys
+// 0.306 -> 0.335 ms per pass at 2^26).
+#ifndef CUSORT_PREFETCH
+#define CUSORT_PREFETCH 0
+#endif
+
+template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_>
 struct OnesweepCfg {
   static constexpr int KB = KB_, VB = VB_, THREADS = THREADS_, KPT = KPT_, MINB = MINB_;
-  static constexpr int RANK_MODE = CUSORT_RANK_MODE;
+  static constexpr bool FLOAT_KEY = FLOAT_KEY_;
+  // Measured on B200 (2^26 items): mode 4 is fastest for pairs and 8-byte
+  // keys; for keys-only <= 4 bytes its extra registers spill and mode 3 wins.
+  static constexpr int RANK_MODE =
+      CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE : ((VB_ == 0 && KB_ <= 4) ? 3 : 4);
   using WC = WarpCounters<RANK_MODE>;
   using Off = Off_;
   static constexpr int WARPS = THREADS / 32;
   static constexpr int TILE = THREADS * KPT;
-  static constexpr size_t OFF_KEYS = 0;
-  static constexpr size_t OFF_VALS = align_up(OFF_KEYS + (size_t)TILE * KB, 128);
-  static constexpr size_t OFF_WTAB = align_up(OFF_VALS + (size_t)TILE * VB, 128);
+  // One staging buffer = the tile's keys + values.  Two buffers when they fit
+  // in this CTA's share of shared memory: the next tile is then loaded by TMA
+  // while the current one is processed.
+  static constexpr size_t KEYS_BYTES = align_up((size_t)TILE * KB, 128);
+  static constexpr size_t BUF_BYTES = KEYS_BYTES + align_up((size_t)TILE * VB, 128);
+  static constexpr size_t REST_BYTES = align_up((size_t)WARPS * WC::BYTES_PER_WARP, 16) + kRadix * 4 +
+                                       2 * kRadix * sizeof(Off) + 16 * 4 + 32;
+  static constexpr size_t SMEM_PER_CTA = (227 * 1024) / MINB - 1024;
+  static constexpr bool PREFETCH = CUSORT_PREFETCH != 0;
+  static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
+  static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
   static constexpr size_t OFF_GBASE = OFF_TSTART + kRadix * 4;
   static constexpr size_t OFF_GOFF = OFF_GBASE + kRadix * sizeof(Off);
   static constexpr size_t OFF_MISC = OFF_GOFF + kRadix * sizeof(Off);
   static constexpr size_t OFF_MBAR = OFF_MISC + 16 * 4;
-  static constexpr size_t SMEM_BYTES = OFF_MBAR + 16;
+  static constexpr size_t SMEM_BYTES = OFF_MBAR + 2 * 8;
   static_assert(THREADS >= kRadix && THREADS % 32 == 0, "need >= 256 threads");
   static_assert(TILE * (KB + VB) < (1 << 20), "mbarrier tx-count limit");
   static_assert(32 * KPT < (1 << 24), "rank packing");
@@ -329,18 +443,18 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   using V = typename dev::UIntOf<(CFG::VB ? CFG::VB : 1)>::T;
   using Off = typename CFG::Off;
   using DB = DescBits<Off>;
+  using WC = typename CFG::WC;
   constexpr int THREADS = CFG::THREADS, KPT = CFG::KPT, TILE = CFG::TILE, WARPS = CFG::WARPS;
+  constexpr int NBUF = CFG::NBUF;
   constexpr bool HAS_V = CFG::VB > 0;
 
   extern __shared__ __align__(128) uint8_t smem[];
-  K* s_keys = reinterpret_cast<K*>(smem + CFG::OFF_KEYS);
-  V* s_vals = reinterpret_cast<V*>(smem + CFG::OFF_VALS);
   uint8_t* s_wtab = smem + CFG::OFF_WTAB;
-  using WC = typename CFG::WC;
   uint32_t* s_tstart = reinterpret_cast<uint32_t*>(smem + CFG::OFF_TSTART);
   Off* s_gbase = reinterpret_cast<Off*>(smem + CFG::OFF_GBASE);
   Off* s_goff = reinterpret_cast<Off*>(smem + CFG::OFF_GOFF);
-  uint32_t* s_misc = reinterpret_cast<uint32_t*>(smem + CFG::OFF_MISC);  // [0] ticket [1] abort [2..9] scan
+  // [0] first ticket, [1] next ticket, [2] abort flag, [3] prefetch in flight, [4..11] scan partials
+  uint32_t* s_misc = reinterpret_cast<uint32_t*>(smem + CFG::OFF_MISC);
   uint64_t* s_mbar = reinterpret_cast<uint64_t*>(smem + CFG::OFF_MBAR);
 
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
@@ -350,18 +464,41 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   const V* vals_in = static_cast<const V*>(a.vals_in);
   V* vals_out = static_cast<V*>(a.vals_out);
   Off* desc = static_cast<Off*>(a.desc);
+  const uint32_t num_tiles = a.num_tiles;
+  const bool tma_ok = a.tma_keys && (!HAS_V || a.tma_vals);
+  const uint64_t pol = dev::l2_policy_evict_first();
+
+  // A tile is staged by TMA when it is full and both inputs are 16-byte aligned.
+  auto tma_tile = [&](uint32_t t) { return tma_ok && t < num_tiles && (uint64_t)(t + 1) * TILE <= a.n; };
+  auto issue_tma = [&](uint32_t t, int buf) {
+    const uint64_t base = (uint64_t)t * TILE;
+    uint8_t* bp = smem + (size_t)buf * CFG::BUF_BYTES;
+    dev::mbar_arrive_expect_tx(s_mbar + buf, (uint32_t)TILE * (CFG::KB + CFG::VB));
+    dev::tma_load_1d(bp, keys_in + base, (uint32_t)TILE * CFG::KB, s_mbar + buf, pol);
+    if constexpr (HAS_V) dev::tma_load_1d(bp + CFG::KEYS_BYTES, vals_in + base, (uint32_t)TILE * CFG::VB, s_mbar + buf, pol);
+  };
+  // Bounded wait for a buffer's bulk copy; false if it timed out.
+  auto wait_tma = [&](int buf, uint32_t parity) {
+    dev::SpinGuard guard;
+    while (!dev::mbar_try_wait(s_mbar + buf, parity))
+      if (guard.expired(nullptr, a.spin_limit_ns)) return false;
+    return true;
+  };
 
   if (tid == 0) {
     dev::mbar_init(s_mbar, 1);
+    dev::mbar_init(s_mbar + 1, 1);
     dev::fence_mbar_init();
-    s_misc[1] = 0;
+    s_misc[2] = 0;
+    s_misc[3] = 0;
   }
   dev::pdl_wait();
   dev::pdl_launch_dependents();
 
   // Global exclusive offset of every digit for this pass (from the upfront
-  // histogram), computed once per CTA.
+  // histogram), computed once per CTA; the first tile ticket is taken here.
   {
+    if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
     Off cv = (tid < kRadix) ? static_cast<const Off*>(a.g_hist_pass)[tid] : Off(0);
     Off incl = cv;
 #pragma unroll
@@ -376,45 +513,70 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       for (uint32_t w = 0; w < warp; ++w) pre += s_goff[w];
       s_gbase[tid] = pre + incl - cv;
     }
-    __syncthreads();
   }
-
-  const uint64_t pol = dev::l2_policy_evict_first();
-  uint32_t phase = 0;
+  uint32_t cur = s_misc[0];
+  uint32_t pending = 0;  // thread 0: ticket requested one tile ahead (prefetch mode)
+  if (CFG::PREFETCH && tid == 0) {
+    if (NBUF == 2 && tma_tile(cur)) issue_tma(cur, 0);
+    pending = atomicAdd(a.tile_counter, 1u);
+  }
+  uint32_t parity = 0u;  // bit b: phase parity of buffer b's mbarrier
+  int b = 0;
   const uint32_t lt = dev::lanemask_lt();
 
-  for (;;) {
-    if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
-    WC::zero(s_wtab, warp, lane);
-    __syncthreads();
-    const uint32_t tile = s_misc[0];
-    if (tile >= a.num_tiles) break;
+  for (bool first = true;; first = false) {
+    if constexpr (!CFG::PREFETCH) {
+      // Ticket for this tile, taken when the CTA is ready for it.
+      if (!first) {
+        if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
+        WC::zero(s_wtab, warp, lane);
+        __syncthreads();
+        cur = s_misc[0];
+      } else {
+        WC::zero(s_wtab, warp, lane);
+        __syncthreads();
+      }
+    }
+    if (cur >= num_tiles) break;
+    uint32_t nxt = 0;
+    if constexpr (CFG::PREFETCH) {
+      WC::zero(s_wtab, warp, lane);
+      if (tid == 0) {
+        s_misc[1] = pending;
+        s_misc[3] = 0;
+      }
+      __syncthreads();  // previous tile fully written out; next ticket visible
+      nxt = s_misc[1];
+      if (tid == 0) {
+        if (NBUF == 2 && tma_tile(nxt)) {
+          issue_tma(nxt, b ^ 1);  // its buffer held the previous tile, consumed before the barrier
+          s_misc[3] = 1;
+        }
+        pending = atomicAdd(a.tile_counter, 1u);
+      }
+    }
+    const uint32_t tile = cur;
     const uint64_t base = (uint64_t)tile * TILE;
     const uint32_t valid = (uint32_t)((a.n - base) < (uint64_t)TILE ? (a.n - base) : (uint64_t)TILE);
     const bool publish = (int64_t)tile != a.skip_tile;
+    K* s_keys = reinterpret_cast<K*>(smem + (size_t)b * CFG::BUF_BYTES);
+    V* s_vals = reinterpret_cast<V*>(smem + (size_t)b * CFG::BUF_BYTES + CFG::KEYS_BYTES);
 
-    // ---- 1. stage the tile in shared memory
-    if (valid == (uint32_t)TILE && a.tma_keys && (!HAS_V || a.tma_vals)) {
-      if (tid == 0) {
-        dev::mbar_arrive_expect_tx(s_mbar, (uint32_t)TILE * (CFG::KB + CFG::VB));
-        dev::tma_load_1d(s_keys, keys_in + base, (uint32_t)TILE * CFG::KB, s_mbar, pol);
-        if constexpr (HAS_V) dev::tma_load_1d(s_vals, vals_in + base, (uint32_t)TILE * CFG::VB, s_mbar, pol);
-      }
-      dev::SpinGuard guard;
-      bool ok = true;
-      while (!dev::mbar_try_wait(s_mbar, phase)) {
-        if (guard.expired(nullptr, a.spin_limit_ns)) {
-          ok = false;
-          break;
-        }
-      }
-      phase ^= 1u;
+    // ---- 1. the tile's keys/values in shared memory
+    if (tma_tile(tile)) {
+      if (NBUF == 1 && tid == 0) issue_tma(tile, 0);
+      const bool ok = wait_tma(b, (parity >> b) & 1u);
+      parity ^= 1u << b;
       if (!ok) {
         atomicOr(a.status, kStatusTmaTimeout);
-        s_misc[1] = 1;
+        s_misc[2] = 1;
       }
       __syncthreads();
-      if (s_misc[1]) break;
+      if (s_misc[2]) {
+        // Give the other buffer's copy, if one is in flight, a bounded wait.
+        if (NBUF == 2 && s_misc[3]) wait_tma(b ^ 1, (parity >> (b ^ 1)) & 1u);
+        break;
+      }
     } else {
       for (uint32_t i = tid; i < valid; i += THREADS) {
         s_keys[i] = keys_in[base + i];
@@ -423,7 +585,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       __syncthreads();
     }
 
-    // ---- 2. load to registers, digit, warp ranking
+    // ---- 2. registers, digits, warp ranking
     K key[KPT];
     uint32_t dr[KPT];  // digit | (rank within warp << 8)
     V val[HAS_V ? KPT : 1];
@@ -432,13 +594,16 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     for (int s = 0; s < KPT; ++s) {
       const uint32_t idx = wfirst + s * 32 + lane;
       key[s] = s_keys[idx];
-      dr[s] = (idx < valid) ? dev::digit_of<K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+      dr[s] = (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
       if constexpr (HAS_V) val[s] = s_vals[idx];
     }
+    constexpr bool EARLY = CFG::RANK_MODE == 4;
+    if constexpr (EARLY) {
 #pragma unroll
-    for (int s = 0; s < KPT; ++s) {
-      const uint32_t r = WC::rank(s_wtab, warp, dr[s], lane, lt);
-      dr[s] |= r << 8;
+      for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, dr[s]);
+    } else {
+      uint32_t prev = 0;
+      RankSlots<CFG::RANK_MODE, 0, KPT>::run(s_wtab, warp, dr, lane, lt, prev);
     }
     __syncthreads();
 
@@ -456,12 +621,15 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         dev::st_relaxed(desc + (size_t)tile * kRadix + tid,
                         DB::make(a.pass, tile == 0 ? kDescInclusive : kDescAggregate, (Off)cnt));
     }
-    const uint32_t incl = dev::warp_inclusive_scan(cnt, lane);
-    if (lane == 31 && warp < kRadix / 32) s_misc[2 + warp] = incl;
+    uint32_t incl = 0;
+    if (warp < kRadix / 32) {
+      incl = dev::warp_inclusive_scan(cnt, lane);
+      if (lane == 31) s_misc[4 + warp] = incl;
+    }
     __syncthreads();
     if (tid < kRadix) {
       uint32_t pre = 0;
-      for (uint32_t w = 0; w < warp; ++w) pre += s_misc[2 + w];
+      for (uint32_t w = 0; w < warp; ++w) pre += s_misc[4 + w];
       const uint32_t ts = pre + incl - cnt;
       s_tstart[tid] = ts;
 #pragma unroll 4
@@ -470,11 +638,22 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     __syncthreads();
 
     // ---- 4. reorder in shared memory (tile sorted by digit, stable)
+    if constexpr (EARLY) {
+      // rank against the per-warp position counters, store at once
+      uint32_t prev = 0;
+      static_for<0, KPT>([&](auto sc) {
+        constexpr int S = decltype(sc)::value;
+        const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, dr[S], lane, lt, prev);
+        s_keys[pos] = key[S];
+        if constexpr (HAS_V) s_vals[pos] = val[S];
+      });
+    } else {
 #pragma unroll
-    for (int s = 0; s < KPT; ++s) {
-      const uint32_t pos = WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8);
-      s_keys[pos] = key[s];
-      if constexpr (HAS_V) s_vals[pos] = val[s];
+      for (int s = 0; s < KPT; ++s) {
+        const uint32_t pos = WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8);
+        s_keys[pos] = key[s];
+        if constexpr (HAS_V) s_vals[pos] = val[s];
+      }
     }
 
     // ---- 5. decoupled lookback
@@ -490,13 +669,23 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     __syncthreads();
 
     // ---- 6. coalesced scatter
-    for (uint32_t j = tid; j < valid; j += THREADS) {
+    auto put_one = [&](uint32_t j) {
       const K k = s_keys[j];
-      const Off dst = s_goff[dev::digit_of<K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+      const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
       keys_out[dst] = k;
       if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+    };
+    if (valid == (uint32_t)TILE) {
+#pragma unroll
+      for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS);
+    } else {
+      for (uint32_t j = tid; j < valid; j += THREADS) put_one(j);
     }
-    dev::fence_proxy_async_smem();
+    dev::fence_proxy_async_smem();  // before the buffer is refilled by TMA
+    if constexpr (CFG::PREFETCH) {
+      cur = nxt;
+      if (NBUF == 2) b ^= 1;
+    }
   }
 }
 

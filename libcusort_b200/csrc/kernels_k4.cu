@@ -3,7 +3,8 @@
 #include "cusort_instances.cuh"
 
 namespace cusort_b200 {
-bool get_kernels_k4(int value_bytes, int off_bytes, KernelInfo* onesweep, KernelInfo* histogram) {
-  return get_kernels_impl<4>(value_bytes, off_bytes, onesweep, histogram);
+bool get_kernels_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep,
+                    KernelInfo* histogram) {
+  return get_kernels_impl<4>(value_bytes, off_bytes, float_key, onesweep, histogram);
 }
 }  // namespace cusort_b200
