@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--total-log2n", type=int, default=None,
+                    help="N>1: fix the global item count at 2^this (strong scaling) instead of 2^log2n per GPU")
     ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs"], default=None,
                     help="only run --warmup + --steps sorts of this case (for ncu captures)")
     return ap.parse_args()

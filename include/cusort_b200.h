@@ -145,6 +145,39 @@ cudaError_t cusort_sort_db_noalloc(cusort_key_type key_type, cusort_double_buffe
                                    cusort_double_buffer* d_values, int64_t num_items, int begin_bit, int end_bit,
                                    int descending, cudaStream_t stream);
 
+/* ---- sharded multi-GPU sort over NCCL (no counterpart in the reference,
+ *      which is single-GPU only) ------------------------------------------
+ * One process (or thread) per GPU.  Rank r passes its contiguous slice of
+ * the global input (global order = rank-major, then local index); it gets
+ * back a contiguous part of the globally sorted sequence (ranks' outputs
+ * concatenated in rank order are the global result), stable by global index.
+ * Steps: most-significant-digit counts, ncclAllGather of G x 256 counts, a
+ * digit -> owner plan computed identically on every rank, a stable local
+ * partition pass, a grouped ncclSend/ncclRecv all-to-all of keys and values,
+ * and a stable local sort of the received items.
+ *
+ * cusort_mgpu_unique_id: on one rank; the caller broadcasts the 128 bytes.
+ * cusort_mgpu_comm_init: every rank, with its GPU current.
+ * cusort_mgpu_plan: host-only planning step (exposed for tests and tools):
+ *   all_counts[r*256 + d] = rank r's count of owner digit d; fills the digit
+ *   owners (256), this rank's send and receive counts per peer, and every
+ *   rank's receive total.  Returns 0 on success.
+ * cusort_mgpu_sort: two-phase temp protocol as the single-GPU calls (the size
+ *   depends on the communicator's size, n_local and out_capacity).  It
+ *   synchronises `stream` once (to read the gathered counts).  Returns
+ *   cudaErrorInvalidValue on every rank, before any data exchange, when some
+ *   rank's share would exceed out_capacity.  *n_out receives this rank's
+ *   item count.  value_bytes 0 = keys only. */
+cudaError_t cusort_mgpu_unique_id(unsigned char* id128);
+cudaError_t cusort_mgpu_comm_init(void** comm, const unsigned char* id128, int nranks, int rank);
+cudaError_t cusort_mgpu_comm_destroy(void* comm);
+int cusort_mgpu_plan(const uint64_t* all_counts, int nranks, int rank, int* digit_owner, int64_t* send_counts,
+                     int64_t* recv_counts, int64_t* recv_totals);
+cudaError_t cusort_mgpu_sort(void* comm, void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                             size_t value_bytes, const void* d_keys_in, const void* d_values_in, int64_t n_local,
+                             void* d_keys_out, void* d_values_out, int64_t out_capacity, int64_t* n_out,
+                             int begin_bit, int end_bit, int descending, cudaStream_t stream);
+
 /* ---- library state, status and diagnostics (no reference counterpart;
  *      the reference has compile-time macros only, libcusort.cuh:119-148) -- */
 

@@ -42,6 +42,13 @@ SIGNATURES = {
     "cusort_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_db_noalloc": (_i, [_i, _P_DB, _sz, _P_DB, _i64, _i, _i, _i, _vp]),
+    "cusort_mgpu_unique_id": (_i, [C.c_char_p]),
+    "cusort_mgpu_comm_init": (_i, [C.POINTER(C.c_void_p), C.c_char_p, _i, _i]),
+    "cusort_mgpu_comm_destroy": (_i, [_vp]),
+    "cusort_mgpu_plan": (_i, [C.POINTER(C.c_uint64), _i, _i, C.POINTER(_i), C.POINTER(_i64), C.POINTER(_i64),
+                              C.POINTER(_i64)]),
+    "cusort_mgpu_sort": (_i, [_vp, _vp, _P_SZ, _i, _sz, _vp, _vp, _i64, _vp, _vp, _i64, C.POINTER(_i64), _i, _i,
+                              _i, _vp]),
     "cusort_version": (C.c_char_p, []),
     "cusort_set_launch_mode": (_i, [_i]),
     "cusort_read_device_status": (_i, [_vp, C.POINTER(_u32), _vp]),

@@ -509,6 +509,45 @@ static cudaError_t sort_impl(const SortCall& c) {
   return cudaSuccess;
 }
 
+// Counts of one digit (bits [begin_bit, end_bit), at most 8 bits) of the
+// twiddled keys into d_counts[256] (u64), using the all-pass histogram kernel
+// with a single pass.  Used by the multi-GPU sort to plan the exchange.
+cudaError_t digit_counts_u64(int kt, bool desc, const void* keys, int64_t n, int begin_bit, int end_bit,
+                             unsigned long long* d_counts, cudaStream_t stream) {
+  const int kb = key_bytes_of(kt);
+  if (kb == 0 || begin_bit < 0 || end_bit <= begin_bit || end_bit - begin_bit > 8 || end_bit > 8 * kb)
+    return cudaErrorInvalidValue;
+  CUSORT_TRY(cudaMemsetAsync(d_counts, 0, kRadix * sizeof(unsigned long long), stream));
+  if (n <= 0) return cudaSuccess;
+  Plan p;
+  // Any n >= 2^30 selects 64-bit counters; the onesweep kernel of this plan is unused.
+  if (!make_plan(kt, 0, desc, std::max<uint64_t>((uint64_t)n, 1ull << 30), begin_bit, end_bit, false, &p))
+    return cudaErrorInvalidValue;
+  int dev = 0, sms = 0, occ_h = 0;
+  CUSORT_TRY(cudaGetDevice(&dev));
+  CUSORT_TRY(get_sm_count(dev, &sms));
+  CUSORT_TRY(get_occupancy(dev, p.hist, &occ_h));
+  HistArgs h = {};
+  h.keys = keys;
+  h.n = (uint64_t)n;
+  h.tw_c = p.tw_c;
+  h.tw_f = p.tw_f;
+  h.begin_bit = (uint32_t)begin_bit;
+  h.num_passes = 1;
+  h.last_mask = p.last_mask;
+  h.g_hist = d_counts;
+  const uint64_t vec = (uint64_t)n * kb / 16 + 1;
+  const uint64_t want = (vec + p.hist.tile - 1) / p.hist.tile;
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ_h, want));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)p.hist.threads);
+  cfg.dynamicSmemBytes = p.hist.smem;
+  cfg.stream = stream;
+  void* args[1] = {&h};
+  return cudaLaunchKernelExC(&cfg, p.hist.func, args);
+}
+
 // DoubleBuffer sort whose temp storage is a caller-provided scratch region
 // of `scratch_bytes` (used by the no-allocation entry point): rejects calls
 // whose temp storage would not fit, and always launches directly.

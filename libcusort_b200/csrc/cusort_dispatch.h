@@ -30,4 +30,8 @@ cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type
                                struct cusort_double_buffer* keys, struct cusort_double_buffer* values,
                                int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
 
+// Single-digit counts (u64[256]) of the twiddled keys (cusort_api.cu).
+cudaError_t digit_counts_u64(int key_type, bool descending, const void* keys, int64_t num_items, int begin_bit,
+                             int end_bit, unsigned long long* d_counts, cudaStream_t stream);
+
 }  // namespace cusort_b200

@@ -1,0 +1,323 @@
+// cusort_mgpu.cu -- sharded multi-GPU sort over NCCL (one process or thread
+// per GPU).  No counterpart in the reference, which is single-GPU only.
+//
+// Every rank holds a contiguous slice of the global input (global index =
+// rank-major, then local index).  Per call:
+//   1. count the most significant (up to 8-bit) digit of the twiddled keys;
+//   2. all-gather the G x 256 counts (ncclAllGather);
+//   3. on the host, every rank derives the same digit -> owner plan
+//      (cusort_mgpu_plan): digits go to ranks in order, each by the midpoint
+//      of its share of the global count, so rank q owns a contiguous digit
+//      range and the ranks' outputs concatenate to the global order;
+//   4. stably partition the local slice by that digit (one onesweep pass);
+//   5. exchange keys and values (grouped ncclSend/ncclRecv, all-to-all); the
+//      receiver lays the pieces out by source rank, i.e. in global index order;
+//   6. stably sort the received items on all key bits.
+// Equal keys therefore end up in global input order (stable across ranks).
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "../../include/cusort_b200.h"
+#include "cusort_dispatch.h"
+
+namespace {
+
+int key_bytes(int kt) {
+  switch (kt) {
+    case CUSORT_KEY_U8: case CUSORT_KEY_I8: return 1;
+    case CUSORT_KEY_U16: case CUSORT_KEY_I16: return 2;
+    case CUSORT_KEY_U32: case CUSORT_KEY_I32: case CUSORT_KEY_F32: return 4;
+    case CUSORT_KEY_U64: case CUSORT_KEY_I64: case CUSORT_KEY_F64: return 8;
+    default: return 0;
+  }
+}
+size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+cudaError_t nccl_to_cuda(ncclResult_t r) {
+  if (r == ncclSuccess) return cudaSuccess;
+  if (r == ncclInvalidArgument || r == ncclInvalidUsage) return cudaErrorInvalidValue;
+  return cudaErrorUnknown;
+}
+
+struct MgpuLayout {
+  size_t counts, all_counts, part_k, part_v, alt_k, alt_v, sort_tmp, sort_tmp_bytes, total;
+};
+
+// Temp storage of one call; the local sorts' sizes come from this library's
+// own size queries.
+cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, int begin, int end, bool desc,
+                   MgpuLayout* L) {
+  const int kb = key_bytes(kt);
+  const int msd_begin = std::max(begin, end - 8);
+  size_t part_tmp = 0, final_tmp = 0, single_tmp = 0;
+  cusort_double_buffer kd = {}, vd = {};
+  cudaError_t e;
+  if (vb) {
+    e = desc ? cusort_sort_pairs_descending(nullptr, &part_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr,
+                                            nullptr, n_local, msd_begin, end, nullptr)
+             : cusort_sort_pairs(nullptr, &part_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr, nullptr,
+                                 n_local, msd_begin, end, nullptr);
+    if (e) return e;
+    e = desc ? cusort_sort_pairs_descending_db(nullptr, &final_tmp, (cusort_key_type)kt, &kd, vb, &vd, cap, begin,
+                                               end, nullptr)
+             : cusort_sort_pairs_db(nullptr, &final_tmp, (cusort_key_type)kt, &kd, vb, &vd, cap, begin, end, nullptr);
+    if (e) return e;
+    e = cusort_sort_pairs(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr, nullptr,
+                          n_local, begin, end, nullptr);
+  } else {
+    e = cusort_sort_keys(nullptr, &part_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, msd_begin, end, nullptr);
+    if (e) return e;
+    e = cusort_sort_keys_db(nullptr, &final_tmp, (cusort_key_type)kt, &kd, cap, begin, end, nullptr);
+    if (e) return e;
+    e = cusort_sort_keys(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, begin, end, nullptr);
+  }
+  if (e) return e;
+  size_t o = 0;
+  L->counts = o;
+  o += a256(256 * 8);
+  L->all_counts = o;
+  o += a256((size_t)nranks * 256 * 8);
+  L->part_k = o;
+  o += a256((size_t)n_local * kb);
+  L->part_v = o;
+  o += a256((size_t)n_local * vb);
+  L->alt_k = o;
+  o += a256((size_t)cap * kb);
+  L->alt_v = o;
+  o += a256((size_t)cap * vb);
+  L->sort_tmp = o;
+  L->sort_tmp_bytes = std::max(std::max(part_tmp, final_tmp), std::max<size_t>(single_tmp, 1));
+  o += a256(L->sort_tmp_bytes);
+  L->total = o;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cusort_mgpu_plan(const uint64_t* all_counts, int nranks, int rank, int* digit_owner, int64_t* send_counts,
+                     int64_t* recv_counts, int64_t* recv_totals) {
+  if (!all_counts || nranks < 1 || rank < 0 || rank >= nranks) return 1;
+  uint64_t total[256] = {};
+  uint64_t N = 0;
+  for (int r = 0; r < nranks; ++r)
+    for (int d = 0; d < 256; ++d) total[d] += all_counts[(size_t)r * 256 + d];
+  for (int d = 0; d < 256; ++d) N += total[d];
+  int owner[256];
+  uint64_t cum = 0;
+  for (int d = 0; d < 256; ++d) {
+    // owner by the midpoint of the digit's share of the global count
+    const long double mid = (long double)cum + (long double)total[d] / 2.0L;
+    int q = (N == 0) ? 0 : (int)((mid * nranks) / (long double)N);
+    owner[d] = std::min(std::max(q, 0), nranks - 1);
+    cum += total[d];
+  }
+  for (int d = 1; d < 256; ++d) owner[d] = std::max(owner[d], owner[d - 1]);  // monotone
+  if (digit_owner) std::memcpy(digit_owner, owner, sizeof(owner));
+  if (send_counts)
+    for (int q = 0; q < nranks; ++q) {
+      int64_t s = 0;
+      for (int d = 0; d < 256; ++d)
+        if (owner[d] == q) s += (int64_t)all_counts[(size_t)rank * 256 + d];
+      send_counts[q] = s;
+    }
+  if (recv_counts)
+    for (int p = 0; p < nranks; ++p) {
+      int64_t s = 0;
+      for (int d = 0; d < 256; ++d)
+        if (owner[d] == rank) s += (int64_t)all_counts[(size_t)p * 256 + d];
+      recv_counts[p] = s;
+    }
+  if (recv_totals)
+    for (int q = 0; q < nranks; ++q) {
+      int64_t s = 0;
+      for (int d = 0; d < 256; ++d)
+        if (owner[d] == q) s += (int64_t)total[d];
+      recv_totals[q] = s;
+    }
+  return 0;
+}
+
+cudaError_t cusort_mgpu_unique_id(unsigned char* id) {
+  if (!id) return cudaErrorInvalidValue;
+  ncclUniqueId u;
+  ncclResult_t r = ncclGetUniqueId(&u);
+  if (r != ncclSuccess) return nccl_to_cuda(r);
+  static_assert(sizeof(u) == 128, "NCCL unique id size");
+  std::memcpy(id, &u, sizeof(u));
+  return cudaSuccess;
+}
+
+cudaError_t cusort_mgpu_comm_init(void** comm, const unsigned char* id, int nranks, int rank) {
+  if (!comm || !id || nranks < 1 || rank < 0 || rank >= nranks) return cudaErrorInvalidValue;
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclComm_t c = nullptr;
+  ncclResult_t r = ncclCommInitRank(&c, nranks, u, rank);
+  if (r != ncclSuccess) return nccl_to_cuda(r);
+  *comm = c;
+  return cudaSuccess;
+}
+
+cudaError_t cusort_mgpu_comm_destroy(void* comm) {
+  if (!comm) return cudaErrorInvalidValue;
+  return nccl_to_cuda(ncclCommDestroy(static_cast<ncclComm_t>(comm)));
+}
+
+cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusort_key_type key_type,
+                             size_t value_bytes, const void* d_keys_in, const void* d_values_in, int64_t n_local,
+                             void* d_keys_out, void* d_values_out, int64_t out_capacity, int64_t* n_out,
+                             int begin_bit, int end_bit, int descending, cudaStream_t stream) {
+  const int kt = (int)key_type;
+  const int kb = key_bytes(kt);
+  const size_t vb = value_bytes;
+  if (!comm || !temp_bytes || kb == 0) return cudaErrorInvalidValue;
+  if (vb != 0 && vb != 1 && vb != 2 && vb != 4 && vb != 8 && vb != 16) return cudaErrorInvalidValue;
+  if (begin_bit < 0 || end_bit < 0 || begin_bit > end_bit || end_bit > 8 * kb) return cudaErrorInvalidValue;
+  if (n_local < 0 || out_capacity < 0) return cudaErrorInvalidValue;
+  ncclComm_t nc = static_cast<ncclComm_t>(comm);
+  int nranks = 0, rank = 0;
+  cudaError_t e = nccl_to_cuda(ncclCommCount(nc, &nranks));
+  if (e) return e;
+  e = nccl_to_cuda(ncclCommUserRank(nc, &rank));
+  if (e) return e;
+  const bool desc = descending != 0;
+
+  if (begin_bit == end_bit) {
+    // Zero-width key range: the global order is the input order; every rank
+    // keeps its slice.
+    if (!d_temp) {
+      *temp_bytes = 1;
+      return cudaSuccess;
+    }
+    if (n_local > out_capacity) return cudaErrorInvalidValue;
+    if (n_local > 0) {
+      e = cudaMemcpyAsync(d_keys_out, d_keys_in, (size_t)n_local * kb, cudaMemcpyDeviceToDevice, stream);
+      if (!e && vb) e = cudaMemcpyAsync(d_values_out, d_values_in, (size_t)n_local * vb, cudaMemcpyDeviceToDevice, stream);
+      if (e) return e;
+    }
+    if (n_out) *n_out = n_local;
+    return cudaSuccess;
+  }
+
+  MgpuLayout L;
+  e = layout(kt, vb, n_local, out_capacity, nranks, begin_bit, end_bit, desc, &L);
+  if (e) return e;
+  if (!d_temp) {
+    *temp_bytes = L.total;
+    return cudaSuccess;
+  }
+  if (*temp_bytes < L.total) return cudaErrorInvalidValue;
+  uint8_t* t = static_cast<uint8_t*>(d_temp);
+  void* stmp = t + L.sort_tmp;
+  size_t stmp_bytes = L.sort_tmp_bytes;
+
+  if (nranks == 1) {
+    if (n_local > out_capacity) return cudaErrorInvalidValue;
+    if (vb)
+      e = desc ? cusort_sort_pairs_descending(stmp, &stmp_bytes, key_type, d_keys_in, d_keys_out, vb, d_values_in,
+                                              d_values_out, n_local, begin_bit, end_bit, stream)
+               : cusort_sort_pairs(stmp, &stmp_bytes, key_type, d_keys_in, d_keys_out, vb, d_values_in, d_values_out,
+                                   n_local, begin_bit, end_bit, stream);
+    else
+      e = desc ? cusort_sort_keys_descending(stmp, &stmp_bytes, key_type, d_keys_in, d_keys_out, n_local, begin_bit,
+                                             end_bit, stream)
+               : cusort_sort_keys(stmp, &stmp_bytes, key_type, d_keys_in, d_keys_out, n_local, begin_bit, end_bit,
+                                  stream);
+    if (e) return e;
+    if (n_out) *n_out = n_local;
+    return cudaSuccess;
+  }
+
+  // 1-2. digit counts, all-gathered
+  const int msd_begin = std::max(begin_bit, end_bit - 8);
+  unsigned long long* counts = reinterpret_cast<unsigned long long*>(t + L.counts);
+  unsigned long long* all_counts = reinterpret_cast<unsigned long long*>(t + L.all_counts);
+  e = cusort_b200::digit_counts_u64(kt, desc, d_keys_in, n_local, msd_begin, end_bit, counts, stream);
+  if (e) return e;
+  e = nccl_to_cuda(ncclAllGather(counts, all_counts, 256, ncclUint64, nc, stream));
+  if (e) return e;
+  std::vector<uint64_t> h_all((size_t)nranks * 256);
+  e = cudaMemcpyAsync(h_all.data(), all_counts, h_all.size() * 8, cudaMemcpyDeviceToHost, stream);
+  if (e) return e;
+  e = cudaStreamSynchronize(stream);
+  if (e) return e;
+
+  // 3. plan (identical on every rank)
+  std::vector<int64_t> send((size_t)nranks), recv((size_t)nranks), totals((size_t)nranks);
+  if (cusort_mgpu_plan(h_all.data(), nranks, rank, nullptr, send.data(), recv.data(), totals.data()))
+    return cudaErrorInvalidValue;
+  for (int q = 0; q < nranks; ++q)
+    if (totals[q] > out_capacity) return cudaErrorInvalidValue;  // every rank sees it: no rank enters NCCL
+  const int64_t n_recv = totals[rank];
+
+  // 4. stable partition by the owner digit
+  void* part_k = t + L.part_k;
+  void* part_v = t + L.part_v;
+  if (vb)
+    e = desc ? cusort_sort_pairs_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, vb, d_values_in, part_v,
+                                            n_local, msd_begin, end_bit, stream)
+             : cusort_sort_pairs(stmp, &stmp_bytes, key_type, d_keys_in, part_k, vb, d_values_in, part_v, n_local,
+                                 msd_begin, end_bit, stream);
+  else
+    e = desc ? cusort_sort_keys_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin,
+                                           end_bit, stream)
+             : cusort_sort_keys(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin, end_bit, stream);
+  if (e) return e;
+
+  // 5. all-to-all: received pieces in source-rank order.  The receive buffer is
+  //    chosen so that the final sort's last pass lands in the caller's output.
+  const int passes = (end_bit - begin_bit + 7) / 8;
+  const bool recv_in_out = (passes % 2) == 0;
+  uint8_t* rk = static_cast<uint8_t*>(recv_in_out ? d_keys_out : (void*)(t + L.alt_k));
+  uint8_t* ok_ = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_k) : d_keys_out);
+  uint8_t* rv = static_cast<uint8_t*>(recv_in_out ? d_values_out : (void*)(t + L.alt_v));
+  uint8_t* ov = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_v) : d_values_out);
+  {
+    ncclResult_t r = ncclGroupStart();
+    int64_t so = 0, ro = 0;
+    for (int q = 0; q < nranks && r == ncclSuccess; ++q) {
+      if (send[q] > 0) {
+        r = ncclSend(static_cast<uint8_t*>(part_k) + so * kb, (size_t)send[q] * kb, ncclUint8, q, nc, stream);
+        if (r == ncclSuccess && vb)
+          r = ncclSend(static_cast<uint8_t*>(part_v) + so * vb, (size_t)send[q] * vb, ncclUint8, q, nc, stream);
+      }
+      if (r == ncclSuccess && recv[q] > 0) {
+        r = ncclRecv(rk + ro * kb, (size_t)recv[q] * kb, ncclUint8, q, nc, stream);
+        if (r == ncclSuccess && vb) r = ncclRecv(rv + ro * vb, (size_t)recv[q] * vb, ncclUint8, q, nc, stream);
+      }
+      so += send[q];
+      ro += recv[q];
+    }
+    ncclResult_t r2 = ncclGroupEnd();
+    e = nccl_to_cuda(r != ncclSuccess ? r : r2);
+    if (e) return e;
+  }
+
+  // 6. stable local sort of the received items on every key bit
+  if (n_recv >= 2) {
+    cusort_double_buffer kd = {{rk, ok_}, 0};
+    cusort_double_buffer vd = {{rv, ov}, 0};
+    if (vb)
+      e = desc ? cusort_sort_pairs_descending_db(stmp, &stmp_bytes, key_type, &kd, vb, &vd, n_recv, begin_bit,
+                                                 end_bit, stream)
+               : cusort_sort_pairs_db(stmp, &stmp_bytes, key_type, &kd, vb, &vd, n_recv, begin_bit, end_bit, stream);
+    else
+      e = desc ? cusort_sort_keys_descending_db(stmp, &stmp_bytes, key_type, &kd, n_recv, begin_bit, end_bit, stream)
+               : cusort_sort_keys_db(stmp, &stmp_bytes, key_type, &kd, n_recv, begin_bit, end_bit, stream);
+    if (e) return e;
+  } else if (n_recv == 1 && !recv_in_out) {
+    e = cudaMemcpyAsync(d_keys_out, rk, kb, cudaMemcpyDeviceToDevice, stream);
+    if (!e && vb) e = cudaMemcpyAsync(d_values_out, rv, vb, cudaMemcpyDeviceToDevice, stream);
+    if (e) return e;
+  }
+  if (n_out) *n_out = n_recv;
+  return cudaSuccess;
+}
+
+}  // extern "C"

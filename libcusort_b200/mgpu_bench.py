@@ -1,0 +1,158 @@
+"""bench.py's N>1 path: the sharded multi-GPU sort, one rank per GPU.
+
+Weak scaling: every rank sorts 2^log2n int32 keys + uint32 values (its slice
+of the global input, values = global index); value = all ranks' items / the
+slowest rank's time.  --total-log2n instead fixes the global size (strong).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import datetime
+import json
+import os
+import statistics
+from pathlib import Path
+
+
+def _peaks(root: Path):
+    p = root / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+def run(args, torch):
+    import torch.distributed as dist
+
+    from . import mgpu
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # The reference has no multi-GPU mode: rank 0 runs its single-GPU bench, the others exit.
+        if rank != 0:
+            return None
+        import bench
+        torch.cuda.set_device(local)
+        from oracle import oracle as O
+        if not O.ref_available():
+            return {"impl": "reference", "unavailable": "oracle/_ref/libcusort_ref.so was not built"}
+        out = bench.run_single(args, torch)
+        out["note"] = "reference is single-GPU only: rank 0 ran the N=1 workload, other ranks idle"
+        return out
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    sorter = None
+    try:
+        sorter = mgpu.ShardedSorter.from_torch_distributed()
+        if getattr(args, "total_log2n", None):
+            n_total = 1 << args.total_log2n
+            scaling = "strong"
+        else:
+            n_total = (1 << args.log2n) * world
+            scaling = "weak"
+        n_local = n_total // world + (1 if rank < n_total % world else 0)
+        first = rank * (n_total // world) + min(rank, n_total % world)
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + rank)
+        keys = torch.randint(-(2 ** 31), 2 ** 31, (n_local,), dtype=torch.int64, device=dev, generator=g).to(torch.int32)
+        vals = torch.arange(first, first + n_local, dtype=torch.int64, device=dev).to(torch.int32)
+        cap = int(n_local * 1.5) + 65536
+        out_k = torch.empty(cap, dtype=torch.int32, device=dev)
+        out_v = torch.empty(cap, dtype=torch.int32, device=dev)
+
+        def step():
+            return sorter.sort(keys, vals, capacity=cap, out_keys=out_k, out_values=out_v)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            ko, vo = step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([a.elapsed_time(b)], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        ms_step = ms.item() / args.steps
+
+        # verification: each rank sorted, ranks ordered, counts add up
+        n_mine = ko.numel()
+        ok_local = bool((ko[1:] >= ko[:-1]).all().item()) if n_mine > 1 else True
+        lo = ko[0].item() if n_mine else 2 ** 31 - 1
+        hi = ko[-1].item() if n_mine else -(2 ** 31)
+        stats = [None] * world
+        dist.all_gather_object(stats, (n_mine, lo, hi, ok_local, int(n_local)))
+        counts_ok = sum(s[0] for s in stats) == n_total
+        order_ok = all(stats[i][2] <= stats[j][1] for i in range(world) for j in range(i + 1, world)
+                       if stats[i][0] and stats[j][0])
+        sorted_ok = all(s[3] for s in stats)
+
+        # e2e: pinned host slice -> H2D -> sharded sort -> D2H of this rank's part
+        kh = keys.cpu().pin_memory()
+        vh = vals.cpu().pin_memory()
+        okh = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+        ovh = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+        kd, vd = torch.empty_like(keys), torch.empty_like(vals)
+
+        def e2e_step():
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            k2, v2 = sorter.sort(kd, vd, capacity=cap, out_keys=out_k, out_values=out_v)
+            m = k2.numel()
+            okh[:m].copy_(k2, non_blocking=True)
+            ovh[:m].copy_(v2, non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 10))
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a.record()
+        for _ in range(e_steps):
+            e2e_step()
+        b.record()
+        torch.cuda.synchronize()
+        ems = torch.tensor([a.elapsed_time(b)], device=dev)
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e_ms = ems.item() / e_steps
+
+        if rank != 0:
+            return None
+        root = Path(__file__).resolve().parents[1]
+        peak, peak_src = _peaks(root)
+        kb = vb = 4
+        # per-GPU algorithmic bytes: partition pass + 4 local passes (2*(K+V) each) + one histogram read
+        local_bytes = (1 + 4) * 2 * n_local * (kb + vb) + 2 * n_local * kb
+        xchg = n_local * (kb + vb) * (world - 1) / world  # expected bytes each GPU sends over NVLink
+        t_ideal = local_bytes / (peak * 1e9) + xchg / 770e9
+        return {
+            "metric": "Gkeys/s (sharded int32/uint32 SortPairs across GPUs)", "value": n_total / (ms_step * 1e-3) / 1e9,
+            "unit": "Gkeys/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "int32 keys / uint32 values (integer radix)",
+            "data": "synthetic (seeded uniform int32 keys per rank, values = global index)",
+            "config": {"workload": "configs[4]-style sharded global sort, MSD all-gather + NCCL all-to-all + local sort",
+                       "n_total": n_total, "n_per_gpu": n_local, "parallelism": f"shard{world}",
+                       "l2": "inputs per GPU 512 MiB > L2"},
+            "verified": {"ranks_sorted": sorted_ok, "ranks_ordered": order_ok, "counts": counts_ok},
+            "gpu_launches": args.steps * 10,
+            "roofline": {"bound": "hbm+nvlink", "achieved_frac_of_pipeline": t_ideal / (ms_step * 1e-3),
+                         "t_ideal_ms": t_ideal * 1e3, "local_hbm_bytes_per_gpu": local_bytes,
+                         "nvlink_bytes_per_gpu": xchg, "peak_hbm_gbs": peak, "peak_source": peak_src,
+                         "nvlink_gbs": 770.0, "nvlink_source": "measured peer copy per direction on this pool"},
+            "e2e": {"value": n_total / (e_ms * 1e-3) / 1e9, "unit": "Gkeys/s", "ms_per_step": e_ms,
+                    "h2d_bytes_per_step": n_total * (kb + vb), "d2h_bytes_per_step": n_total * (kb + vb)},
+        }
+    finally:
+        if sorter is not None:
+            sorter.close()
+        dist.destroy_process_group()

@@ -1,0 +1,90 @@
+"""Sharded multi-GPU sort on real GPUs through cusort_mgpu_sort.
+
+With one GPU: a 1-rank communicator must give the single-GPU result.  With
+>= 2 GPUs (one process per GPU, NCCL): the ranks' concatenated outputs must
+equal the CPU oracle's stable sort of the global input, bit-exact.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+from libcusort_b200 import mgpu  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+from tests import datagen as D  # noqa: E402
+
+
+def test_single_rank_communicator_matches_oracle():
+    s = mgpu.ShardedSorter(0, 1, mgpu.ShardedSorter.unique_id())
+    try:
+        keys = D.uniform_bits("i32", 300_001, seed=3)
+        vals = np.arange(keys.size, dtype=np.uint32)
+        ko, vo = s.sort(torch.from_numpy(keys).cuda(), torch.from_numpy(vals.view(np.int32)).cuda())
+        ek, ev = O.oracle_sort("i32", keys, vals)
+        assert np.array_equal(ko.cpu().numpy(), ek)
+        assert np.array_equal(vo.cpu().numpy().view(np.uint32), ev)
+    finally:
+        s.close()
+
+
+def _port():
+    so = socket.socket()
+    so.bind(("127.0.0.1", 0))
+    p = so.getsockname()[1]
+    so.close()
+    return p
+
+
+def _worker(rank, world, port, case, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    s = None
+    try:
+        s = mgpu.ShardedSorter.from_torch_distributed()
+        kind, kt, n, begin, end, desc = case
+        keys = D.zipf_table(kt, n, seed=2, distinct=1 << 14) if kind == "zipf" else D.uniform_bits(kt, n, seed=2)
+        gidx = np.arange(n, dtype=np.uint32)
+        sl = np.array_split(np.arange(n), world)[rank]
+        kd = torch.from_numpy(np.ascontiguousarray(keys[sl])).cuda()  # the tensor dtype selects the key type
+        vd = torch.from_numpy(gidx[sl].view(np.int32)).cuda()
+        ko, vo = s.sort(kd, vd, capacity=n, begin_bit=begin, end_bit=end, descending=desc)
+        parts = [None] * world
+        dist.all_gather_object(parts, (ko.cpu().numpy().tobytes(), vo.cpu().numpy().tobytes()))
+        if rank == 0:
+            gk = np.frombuffer(b"".join(p[0] for p in parts), dtype=keys.dtype)
+            gv = np.frombuffer(b"".join(p[1] for p in parts), dtype=np.uint32)
+            ek, ev = O.oracle_sort(kt, keys, gidx, begin, end, desc)
+            q.put(bool(np.array_equal(gk.view(np.uint8), ek.view(np.uint8)) and np.array_equal(gv, ev)))
+    finally:
+        if s is not None:
+            s.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+@pytest.mark.parametrize("case", [
+    ("uniform", "u32", 1 << 20, 0, 32, False),
+    ("uniform", "f32", 777_777, 0, 32, True),
+    ("zipf", "i32", 1 << 20, 0, 32, False),
+    ("uniform", "u32", 500_000, 5, 27, False),
+], ids=lambda c: "-".join(map(str, c)))
+def test_sharded_sort_all_gpus(case):
+    import torch.multiprocessing as mp
+    world = torch.cuda.device_count()
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.start_processes(_worker, args=(world, _port(), case, q), nprocs=world, join=True, start_method="spawn")
+    assert q.get() is True
