@@ -338,6 +338,13 @@ struct RankSlots {
   }
 };
 
+// Tile input path: 1 = streaming loads straight into registers, 0 = TMA bulk
+// copy into shared memory first, -1 = per configuration (measured on B200:
+// direct loads are faster for keys-only, TMA staging for pairs).
+#ifndef CUSORT_DIRECT_LOAD
+#define CUSORT_DIRECT_LOAD -1
+#endif
+
 // Tile prefetch: 1 = take the next tile's ticket one tile ahead and TMA-load
 // it into a second buffer while the current tile is processed.  Off by
 // default: on B200 the early tickets delay those tiles' descriptors and the
@@ -368,6 +375,10 @@ struct OnesweepCfg {
                                        2 * kRadix * sizeof(Off) + 16 * 4 + 32;
   static constexpr size_t SMEM_PER_CTA = (227 * 1024) / MINB - 1024;
   static constexpr bool PREFETCH = CUSORT_PREFETCH != 0;
+  static constexpr bool DIRECT_LOAD = CUSORT_DIRECT_LOAD >= 0 ? (CUSORT_DIRECT_LOAD == 1) : (VB_ == 0 && KB_ <= 4);
+  // 4-byte keys with 4-byte values move through shared memory as one 8-byte
+  // item (one 64-bit store when scattering, one 64-bit load when writing out).
+  static constexpr bool PACKED_KV = (KB_ == 4 && VB_ == 4);
   static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
   static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
@@ -469,7 +480,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   const uint64_t pol = dev::l2_policy_evict_first();
 
   // A tile is staged by TMA when it is full and both inputs are 16-byte aligned.
-  auto tma_tile = [&](uint32_t t) { return tma_ok && t < num_tiles && (uint64_t)(t + 1) * TILE <= a.n; };
+  auto tma_tile = [&](uint32_t t) {
+    return !CFG::DIRECT_LOAD && tma_ok && t < num_tiles && (uint64_t)(t + 1) * TILE <= a.n;
+  };
   auto issue_tma = [&](uint32_t t, int buf) {
     const uint64_t base = (uint64_t)t * TILE;
     uint8_t* bp = smem + (size_t)buf * CFG::BUF_BYTES;
@@ -577,7 +590,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         if (NBUF == 2 && s_misc[3]) wait_tma(b ^ 1, (parity >> (b ^ 1)) & 1u);
         break;
       }
-    } else {
+    } else if constexpr (!CFG::DIRECT_LOAD) {
       for (uint32_t i = tid; i < valid; i += THREADS) {
         s_keys[i] = keys_in[base + i];
         if constexpr (HAS_V) s_vals[i] = vals_in[base + i];
@@ -590,13 +603,40 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     uint32_t dr[KPT];  // digit | (rank within warp << 8)
     V val[HAS_V ? KPT : 1];
     const uint32_t wfirst = warp * (KPT * 32);
+    if constexpr (CFG::DIRECT_LOAD) {
+      const K* kin = keys_in + base + wfirst + lane;
+      const V* vin = vals_in + base + wfirst + lane;
+      if (valid == (uint32_t)TILE) {
 #pragma unroll
-    for (int s = 0; s < KPT; ++s) {
-      const uint32_t idx = wfirst + s * 32 + lane;
-      key[s] = s_keys[idx];
-      dr[s] = (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
-      if constexpr (HAS_V) val[s] = s_vals[idx];
+        for (int s = 0; s < KPT; ++s) {
+          key[s] = dev::ld_cs(kin + s * 32);
+          if constexpr (HAS_V) val[s] = dev::ld_cs(vin + s * 32);
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < KPT; ++s) {
+          const bool in = wfirst + s * 32 + lane < valid;
+          key[s] = in ? dev::ld_cs(kin + s * 32) : K(0);
+          if constexpr (HAS_V) {
+            if (in) val[s] = dev::ld_cs(vin + s * 32);
+          }
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < KPT; ++s) {
+        const uint32_t idx = wfirst + s * 32 + lane;
+        dr[s] = (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+      }
+    } else {
+#pragma unroll
+      for (int s = 0; s < KPT; ++s) {
+        const uint32_t idx = wfirst + s * 32 + lane;
+        key[s] = s_keys[idx];
+        dr[s] = (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+        if constexpr (HAS_V) val[s] = s_vals[idx];
+      }
     }
+    uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
     constexpr bool EARLY = CFG::RANK_MODE == 4;
     if constexpr (EARLY) {
 #pragma unroll
@@ -638,25 +678,37 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     __syncthreads();
 
     // ---- 4. reorder in shared memory (tile sorted by digit, stable)
-    if constexpr (EARLY) {
-      // rank against the per-warp position counters, store at once
-      uint32_t prev = 0;
-      static_for<0, KPT>([&](auto sc) {
-        constexpr int S = decltype(sc)::value;
-        const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, dr[S], lane, lt, prev);
-        s_keys[pos] = key[S];
-        if constexpr (HAS_V) s_vals[pos] = val[S];
-      });
-    } else {
+    auto reorder = [&]() {
+      if constexpr (EARLY) {
+        // rank against the per-warp position counters, store at once
+        uint32_t prev = 0;
+        static_for<0, KPT>([&](auto sc) {
+          constexpr int S = decltype(sc)::value;
+          const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, dr[S], lane, lt, prev);
+          if constexpr (CFG::PACKED_KV) {
+            s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
+          } else {
+            s_keys[pos] = key[S];
+            if constexpr (HAS_V) s_vals[pos] = val[S];
+          }
+        });
+      } else {
 #pragma unroll
-      for (int s = 0; s < KPT; ++s) {
-        const uint32_t pos = WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8);
-        s_keys[pos] = key[s];
-        if constexpr (HAS_V) s_vals[pos] = val[s];
+        for (int s = 0; s < KPT; ++s) {
+          const uint32_t pos = WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8);
+          if constexpr (CFG::PACKED_KV) {
+            s_kv[pos] = make_uint2((uint32_t)key[s], (uint32_t)val[s]);
+          } else {
+            s_keys[pos] = key[s];
+            if constexpr (HAS_V) s_vals[pos] = val[s];
+          }
+        }
       }
-    }
+    };
 
-    // ---- 5. decoupled lookback
+    // ---- 5. decoupled lookback.  The warps that own a digit (0-7) run it
+    // before their own reorder, so its L2 round trips overlap the other
+    // warps' reorder work instead of trailing it.
     if (tid < kRadix) {
       Off excl = 0;
       if (tile > 0) {
@@ -666,14 +718,23 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       }
       s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
     }
+    reorder();
     __syncthreads();
 
     // ---- 6. coalesced scatter
     auto put_one = [&](uint32_t j) {
-      const K k = s_keys[j];
-      const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
-      keys_out[dst] = k;
-      if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+      if constexpr (CFG::PACKED_KV) {
+        const uint2 kv = s_kv[j];
+        const K k = (K)kv.x;
+        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        keys_out[dst] = k;
+        vals_out[dst] = (V)kv.y;
+      } else {
+        const K k = s_keys[j];
+        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        keys_out[dst] = k;
+        if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+      }
     };
     if (valid == (uint32_t)TILE) {
 #pragma unroll
