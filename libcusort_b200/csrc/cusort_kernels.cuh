@@ -56,17 +56,6 @@ __global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a)
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
   const uint32_t P = a.num_passes;
   uint32_t* my_hist = s_hist + rep;
-  auto count = [&](K k) {
-    const K t = dev::twiddle_k<FLOAT_KEY, K>(k, tc, tf);
-#pragma unroll
-    for (int p = 0; p < MAXP; ++p) {
-      if (p < (int)P) {
-        const uint32_t m = (p + 1 == (int)P) ? a.last_mask : 0xffu;
-        const uint32_t d = (uint32_t)(t >> (a.begin_bit + 8 * p)) & m;
-        atomicAdd(my_hist + (p * kRadix + d) * R, 1u);
-      }
-    }
-  };
 
   const K* keys = static_cast<const K*>(a.keys);
   const uint64_t n = a.n;
@@ -78,27 +67,51 @@ __global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a)
   const uint64_t gthreads = (uint64_t)gridDim.x * THREADS;
   const uint64_t gtid = (uint64_t)blockIdx.x * THREADS + tid;
 
-  uint64_t v = gtid;
-  for (; v + (UNROLL - 1) * gthreads < nvec; v += UNROLL * gthreads) {
-    uint4 x[UNROLL];
+  // FULL: every byte of the key is one pass (begin_bit 0, all passes 8 bits
+  // wide) -- the common case -- so digits are constant byte extractions and
+  // the counter offsets compile-time constants.
+  auto run = [&](auto full_tag) {
+    constexpr bool FULL = decltype(full_tag)::value;
+    auto count = [&](K k) {
+      const K t = dev::twiddle_k<FLOAT_KEY, K>(k, tc, tf);
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) x[u] = dev::ld_stream_v4(vec + v + u * gthreads);
+      for (int p = 0; p < MAXP; ++p) {
+        if constexpr (FULL) {
+          const uint32_t d = (uint32_t)(t >> (8 * p)) & 0xffu;
+          atomicAdd(my_hist + (p * kRadix + d) * R, 1u);
+        } else if (p < (int)P) {
+          const uint32_t m = (p + 1 == (int)P) ? a.last_mask : 0xffu;
+          const uint32_t d = (uint32_t)(t >> (a.begin_bit + 8 * p)) & m;
+          atomicAdd(my_hist + (p * kRadix + d) * R, 1u);
+        }
+      }
+    };
+    uint64_t v = gtid;
+    for (; v + (UNROLL - 1) * gthreads < nvec; v += UNROLL * gthreads) {
+      uint4 x[UNROLL];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const K* kk = reinterpret_cast<const K*>(&x[u]);
+      for (int u = 0; u < UNROLL; ++u) x[u] = dev::ld_stream_v4(vec + v + u * gthreads);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const K* kk = reinterpret_cast<const K*>(&x[u]);
+#pragma unroll
+        for (int e = 0; e < PER; ++e) count(kk[e]);
+      }
+    }
+    for (; v < nvec; v += gthreads) {
+      uint4 x = dev::ld_stream_v4(vec + v);
+      const K* kk = reinterpret_cast<const K*>(&x);
 #pragma unroll
       for (int e = 0; e < PER; ++e) count(kk[e]);
     }
-  }
-  for (; v < nvec; v += gthreads) {
-    uint4 x = dev::ld_stream_v4(vec + v);
-    const K* kk = reinterpret_cast<const K*>(&x);
-#pragma unroll
-    for (int e = 0; e < PER; ++e) count(kk[e]);
-  }
-  // Unaligned head and ragged tail, element by element.
-  for (uint64_t i = gtid; i < head; i += gthreads) count(keys[i]);
-  for (uint64_t i = head + nvec * PER + gtid; i < n; i += gthreads) count(keys[i]);
+    // Unaligned head and ragged tail, element by element.
+    for (uint64_t i = gtid; i < head; i += gthreads) count(keys[i]);
+    for (uint64_t i = head + nvec * PER + gtid; i < n; i += gthreads) count(keys[i]);
+  };
+  if (P == (uint32_t)MAXP && a.begin_bit == 0 && a.last_mask == 0xffu)
+    run(std::integral_constant<bool, true>{});
+  else
+    run(std::integral_constant<bool, false>{});
   __syncthreads();
 
   dev::pdl_wait();  // g_hist zeroed by init_kernel
@@ -305,6 +318,28 @@ struct WarpCounters<4> : WarpCounters<3> {
   __device__ __forceinline__ static void count_key(uint8_t* tab, uint32_t warp, uint32_t d) {
     uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
     atomicAdd(cnt + (d >> 1), 1u << ((d & 1u) << 4));
+  }
+};
+
+// Mode 5: mode 4's counting pre-pass and position counters with the peer set
+// found by 8 ballots (ALU only, no shared-memory match table).
+template <>
+struct WarpCounters<5> : WarpCounters<1> {
+  __device__ __forceinline__ static void count_key(uint8_t* tab, uint32_t warp, uint32_t d) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(tab) + warp * (kRadix / 2);
+    atomicAdd(cnt + (d >> 1), 1u << ((d & 1u) << 4));
+  }
+  template <int S>
+  __device__ __forceinline__ static uint32_t rank_slot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                       uint32_t lt, uint32_t&) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(tab) + warp * (kRadix / 2);
+    const uint32_t peers = dev::match_digit_ballot<8>(d);
+    const uint32_t below = __popc(peers & lt);
+    const uint32_t leader = 31u - __clz(peers);
+    const uint32_t sh = (d & 1u) << 4;
+    uint32_t old = dev::atom_add_shared_if(lane == leader, cnt + (d >> 1), (below + 1u) << sh, 0u);
+    old = __shfl_sync(0xffffffffu, old, leader);
+    return ((old >> sh) & 0xffffu) + below;
   }
 };
 
@@ -637,7 +672,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       }
     }
     uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
-    constexpr bool EARLY = CFG::RANK_MODE == 4;
+    constexpr bool EARLY = CFG::RANK_MODE >= 4;
     if constexpr (EARLY) {
 #pragma unroll
       for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, dr[s]);
