@@ -115,6 +115,17 @@ cudaError_t cusort_sort_pairs_descending(void* d_temp_storage, size_t* temp_stor
                                          size_t value_bytes, const void* d_values_in, void* d_values_out,
                                          int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
 
+/* ---- payloads of any width (the reference caps values at 16 bytes,
+ *      libcusort.cuh:2854) ----------------------------------------------
+ * Sorts the keys together with their input index, then gathers the payload
+ * rows (value_bytes each, any size >= 1) by that permutation.  Same ordering,
+ * stability and in/out semantics as cusort_sort_pairs[_descending]; two-phase
+ * temp protocol. */
+cudaError_t cusort_sort_pairs_wide(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                                   const void* d_keys_in, void* d_keys_out, size_t value_bytes,
+                                   const void* d_values_in, void* d_values_out, int64_t num_items, int begin_bit,
+                                   int end_bit, int descending, cudaStream_t stream);
+
 /* ---- sorting without any device allocation ----------------------------
  * No counterpart in the reference (which always takes temp storage from the
  * caller).  For callers that cannot allocate device memory when they need to

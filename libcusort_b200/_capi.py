@@ -41,6 +41,7 @@ SIGNATURES = {
     "cusort_sort_keys_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
+    "cusort_sort_pairs_wide": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _i, _vp]),
     "cusort_sort_db_noalloc": (_i, [_i, _P_DB, _sz, _P_DB, _i64, _i, _i, _i, _vp]),
     "cusort_mgpu_unique_id": (_i, [C.c_char_p]),
     "cusort_mgpu_comm_init": (_i, [C.POINTER(C.c_void_p), C.c_char_p, _i, _i]),

@@ -198,3 +198,25 @@ def test_reference_parity_bit_ranges(kt, begin, end):
     rk, rv, _ = run_ref(kt, keys, vals, begin, end, True)
     ok, ov, _ = run_ours(kt, keys, vals, begin, end, True)
     assert same_bits(rk, ok) and same_bits(rv, ov)
+
+
+# --- payloads wider than 16 bytes (index sort + gather) -------------------------
+@pytest.mark.parametrize("vb", [3, 24, 32, 100])
+@pytest.mark.parametrize("desc", [False, True])
+def test_wide_payloads(vb, desc):
+    from tests.gpu_helpers import DevBuf
+    lib = _capi.load()
+    n = 123_457
+    keys = D.uniform_bits("f32", n, seed=vb)
+    vals = np.random.default_rng(vb).integers(0, 256, size=(n, vb), dtype=np.uint8)
+    kin, kout = DevBuf.from_array(keys), DevBuf(keys.nbytes)
+    vin, vout = DevBuf.from_array(vals), DevBuf(vals.nbytes)
+    nb = C.c_size_t(0)
+    args = (8, kin.ptr, kout.ptr, vb, vin.ptr, vout.ptr, n, 0, 32, int(desc), None)
+    assert lib.cusort_sort_pairs_wide(None, C.byref(nb), *args) == 0
+    temp = DevBuf(nb.value)
+    assert lib.cusort_sort_pairs_wide(temp.ptr, C.byref(nb), *args) == 0
+    torch.cuda.synchronize()
+    ek, ev = O.oracle_sort("f32", keys, vals, 0, 32, desc)
+    assert same_bits(kout.to_array(keys), ek) and same_bits(vout.to_array(vals), ev)
+    assert all(b.guards_ok() for b in (kin, kout, vin, vout, temp))
