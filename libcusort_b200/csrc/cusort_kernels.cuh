@@ -374,10 +374,11 @@ struct RankSlots {
 };
 
 // Tile input path: 1 = streaming loads straight into registers, 0 = TMA bulk
-// copy into shared memory first, -1 = per configuration (measured on B200:
-// direct loads are faster for keys-only, TMA staging for pairs).
+// copy into shared memory first (default: with the large tiles TMA staging
+// is as fast or faster for every width measured), -1 = direct loads for
+// 4-byte keys-only only.
 #ifndef CUSORT_DIRECT_LOAD
-#define CUSORT_DIRECT_LOAD -1
+#define CUSORT_DIRECT_LOAD 0
 #endif
 
 // Tile prefetch: 1 = take the next tile's ticket one tile ahead and TMA-load
@@ -389,14 +390,20 @@ struct RankSlots {
 #define CUSORT_PREFETCH 0
 #endif
 
+// Rank mode per key/value width (measured on B200, see OnesweepCfg).
+#ifndef CUSORT_KEYS_RANK_MODE
+#define CUSORT_KEYS_RANK_MODE 4
+#endif
+#define CUSORT_RANK_MODE_OF(KB, VB) \
+  (CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE : (((VB) == 0 && (KB) <= 4) ? CUSORT_KEYS_RANK_MODE : 4))
+
 template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_>
 struct OnesweepCfg {
   static constexpr int KB = KB_, VB = VB_, THREADS = THREADS_, KPT = KPT_, MINB = MINB_;
   static constexpr bool FLOAT_KEY = FLOAT_KEY_;
   // Measured on B200 (2^26 items): mode 4 is fastest for pairs and 8-byte
   // keys; for keys-only <= 4 bytes its extra registers spill and mode 3 wins.
-  static constexpr int RANK_MODE =
-      CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE : ((VB_ == 0 && KB_ <= 4) ? 3 : 4);
+  static constexpr int RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
   using WC = WarpCounters<RANK_MODE>;
   using Off = Off_;
   static constexpr int WARPS = THREADS / 32;
@@ -414,6 +421,14 @@ struct OnesweepCfg {
   // 4-byte keys with 4-byte values move through shared memory as one 8-byte
   // item (one 64-bit store when scattering, one 64-bit load when writing out).
   static constexpr bool PACKED_KV = (KB_ == 4 && VB_ == 4);
+  // Mode 4 needs a key's digit twice (count, rank); recomputing it from the
+  // key instead of keeping a digit array frees KPT registers, which buys
+  // larger tiles (2 = every width, 1 = keys-only, 0 = never).
+#ifndef CUSORT_RECOMPUTE_DIGIT
+#define CUSORT_RECOMPUTE_DIGIT 2
+#endif
+  static constexpr bool RECOMPUTE_DIGIT =
+      CUSORT_RANK_MODE_OF(KB_, VB_) >= 4 && (CUSORT_RECOMPUTE_DIGIT == 2 || (CUSORT_RECOMPUTE_DIGIT == 1 && VB_ == 0));
   static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
   static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
@@ -634,10 +649,17 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
 
     // ---- 2. registers, digits, warp ranking
+    const uint32_t wfirst_c = warp * (KPT * 32);
     K key[KPT];
-    uint32_t dr[KPT];  // digit | (rank within warp << 8)
+    constexpr bool RECOMP = CFG::RECOMPUTE_DIGIT;
+    uint32_t dr[RECOMP ? 1 : KPT];  // digit | (rank within warp << 8)
+    // digit of slot s (the top digit for slots past the end of the tile)
+    auto digit_at = [&](int s) -> uint32_t {
+      const uint32_t idx = wfirst_c + s * 32 + lane;
+      return (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+    };
     V val[HAS_V ? KPT : 1];
-    const uint32_t wfirst = warp * (KPT * 32);
+    const uint32_t wfirst = wfirst_c;
     if constexpr (CFG::DIRECT_LOAD) {
       const K* kin = keys_in + base + wfirst + lane;
       const V* vin = vals_in + base + wfirst + lane;
@@ -657,17 +679,16 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
           }
         }
       }
+      if constexpr (!RECOMP) {
 #pragma unroll
-      for (int s = 0; s < KPT; ++s) {
-        const uint32_t idx = wfirst + s * 32 + lane;
-        dr[s] = (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+        for (int s = 0; s < KPT; ++s) dr[s] = digit_at(s);
       }
     } else {
 #pragma unroll
       for (int s = 0; s < KPT; ++s) {
         const uint32_t idx = wfirst + s * 32 + lane;
         key[s] = s_keys[idx];
-        dr[s] = (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+        if constexpr (!RECOMP) dr[s] = digit_at(s);
         if constexpr (HAS_V) val[s] = s_vals[idx];
       }
     }
@@ -675,8 +696,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     constexpr bool EARLY = CFG::RANK_MODE >= 4;
     if constexpr (EARLY) {
 #pragma unroll
-      for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, dr[s]);
+      for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
     } else {
+      static_assert(!RECOMP, "digit recomputation needs the early-count rank modes");
       uint32_t prev = 0;
       RankSlots<CFG::RANK_MODE, 0, KPT>::run(s_wtab, warp, dr, lane, lt, prev);
     }
@@ -719,7 +741,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         uint32_t prev = 0;
         static_for<0, KPT>([&](auto sc) {
           constexpr int S = decltype(sc)::value;
-          const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, dr[S], lane, lt, prev);
+          const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev);
           if constexpr (CFG::PACKED_KV) {
             s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
           } else {
