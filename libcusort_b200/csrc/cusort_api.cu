@@ -237,6 +237,7 @@ struct Launch {
     InitArgs init;
     HistArgs hist;
     OnesweepArgs os;
+    FillArgs fill;
   } args;
 };
 
@@ -295,6 +296,22 @@ static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers
     h.last_mask = p.last_mask;
     h.g_hist = g_hist;
     out->push_back(l);
+  }
+  // 1-byte keys, no values, every key bit sorted in one pass: count and fill.
+  if (p.kb == 1 && p.vb == 0 && p.begin == 0 && p.end == 8) {
+    Launch l{};
+    l.func = get_fill_bytes_kernel(p.offb);
+    l.grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * 8, (p.n / 16 + 255) / 256));
+    l.threads = 256;
+    l.smem = 0;
+    l.pdl = true;
+    l.kind = 2;
+    l.args.fill.counts = g_hist;
+    l.args.fill.out = b.k_dst[0];
+    l.args.fill.n = p.n;
+    l.args.fill.xor_c = (uint32_t)p.tw_c;
+    out->push_back(l);
+    return cudaSuccess;
   }
   const int os_grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ_os, p.tiles));
   for (uint32_t pass = 0; pass < p.passes; ++pass) {

@@ -24,6 +24,8 @@ bool get_kernels_k2(int value_bytes, int off_bytes, bool float_key, KernelInfo* 
 bool get_kernels_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 bool get_kernels_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 const void* get_init_kernel();
+// Count-and-fill kernel of 1-byte keys-only full-range sorts (kernels_k1.cu).
+const void* get_fill_bytes_kernel(int off_bytes);
 
 // DoubleBuffer sort with `scratch` as its temp storage (cusort_api.cu).
 cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type, size_t value_bytes, bool descending,

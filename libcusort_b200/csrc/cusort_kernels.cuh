@@ -125,6 +125,60 @@ __global__ void __launch_bounds__(THREADS, 1) histogram_kernel(const HistArgs a)
 }
 
 // ---------------------------------------------------------------------------
+// fill (1-byte keys-only, all 8 bits sorted): the digit is the whole key, so
+// keys with equal digits are bit-identical and the sorted output is every key
+// value repeated by its count -- one histogram read plus this write-only
+// kernel, instead of a ranking pass.  out[i] = (d ^ c) for the digit d whose
+// range [start[d], start[d+1]) holds i.
+// ---------------------------------------------------------------------------
+template <typename Off>
+__global__ void __launch_bounds__(256) fill_bytes_kernel(const FillArgs a) {
+  __shared__ Off s_start[kRadix + 1];
+  __shared__ Off s_part[8];
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  dev::pdl_wait();  // counts from the histogram kernel
+  const Off c = static_cast<const Off*>(a.counts)[tid];
+  Off incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const Off t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= (uint32_t)o) incl += t;
+  }
+  if (lane == 31) s_part[warp] = incl;
+  __syncthreads();
+  Off pre = 0;
+  for (uint32_t w = 0; w < warp; ++w) pre += s_part[w];
+  s_start[tid] = pre + incl - c;
+  if (tid == 0) s_start[kRadix] = (Off)a.n;
+  __syncthreads();
+  uint8_t* out = static_cast<uint8_t*>(a.out);
+  const uint8_t xc = (uint8_t)a.xor_c;
+  auto digit_at = [&](uint64_t i) {  // largest d with start[d] <= i
+    uint32_t lo = 0;
+#pragma unroll
+    for (uint32_t step = 128; step; step >>= 1)
+      if ((uint64_t)s_start[lo + step] <= i) lo += step;
+    return lo;
+  };
+  const uint64_t head = (16 - (reinterpret_cast<uintptr_t>(out) & 15)) & 15;
+  const uint64_t h = head < a.n ? head : a.n;
+  const uint64_t nvec = (a.n - h) / 16;
+  const uint64_t gthreads = (uint64_t)gridDim.x * 256, gtid = (uint64_t)blockIdx.x * 256 + tid;
+  for (uint64_t v = gtid; v < nvec; v += gthreads) {
+    const uint64_t p = h + v * 16;
+    const uint32_t d = digit_at(p);
+    if ((uint64_t)s_start[d + 1] >= p + 16) {
+      const uint32_t b = (uint32_t)(uint8_t)(d ^ xc) * 0x01010101u;
+      *reinterpret_cast<uint4*>(out + p) = make_uint4(b, b, b, b);
+    } else {
+      for (int e = 0; e < 16; ++e) out[p + e] = (uint8_t)(digit_at(p + e) ^ xc);
+    }
+  }
+  for (uint64_t i = gtid; i < h; i += gthreads) out[i] = (uint8_t)(digit_at(i) ^ xc);
+  for (uint64_t i = h + nvec * 16 + gtid; i < a.n; i += gthreads) out[i] = (uint8_t)(digit_at(i) ^ xc);
+}
+
+// ---------------------------------------------------------------------------
 // onesweep: one stable LSD pass over digit (shift, mask).
 //
 // Persistent CTAs take tiles from a global ticket counter (so the lookback

@@ -35,6 +35,13 @@ struct HistArgs {
   void* g_hist;            // OffsetT[num_passes * 256]
 };
 
+struct FillArgs {
+  const void* counts;  // OffsetT[256] digit counts
+  void* out;           // n bytes
+  uint64_t n;
+  uint32_t xor_c;      // key = digit ^ xor_c (1-byte keys have no float twiddle)
+};
+
 struct OnesweepArgs {
   const void* keys_in;
   void* keys_out;

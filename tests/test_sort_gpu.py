@@ -220,3 +220,16 @@ def test_wide_payloads(vb, desc):
     ek, ev = O.oracle_sort("f32", keys, vals, 0, 32, desc)
     assert same_bits(kout.to_array(keys), ek) and same_bits(vout.to_array(vals), ev)
     assert all(b.guards_ok() for b in (kin, kout, vin, vout, temp))
+
+
+# --- 1-byte keys-only over all 8 bits: count-and-fill path ---------------------
+@pytest.mark.parametrize("kt", ["u8", "i8"])
+@pytest.mark.parametrize("desc", [False, True])
+@pytest.mark.parametrize("n", [1, 17, 4095, 1_000_003])
+def test_byte_keys_count_fill(kt, desc, n):
+    keys = D.uniform_bits(kt, n, seed=n)
+    if n > 100:
+        keys[: n // 3] = keys[0]  # one heavy value
+    check(kt, keys, None, desc=desc)
+    check(kt, keys, None, desc=desc, api="db")
+    check(kt, keys, None, desc=desc, offset_items=3)
