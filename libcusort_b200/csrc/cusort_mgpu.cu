@@ -10,15 +10,24 @@
 //      of its share of the global count, so rank q owns a contiguous digit
 //      range and the ranks' outputs concatenate to the global order;
 //   4. stably partition the local slice by that digit (one onesweep pass);
-//   5. exchange keys and values (grouped ncclSend/ncclRecv, all-to-all); the
-//      receiver lays the pieces out by source rank, i.e. in global index order;
+//   5. exchange keys and values, all-to-all; the receiver lays the pieces out
+//      by source rank, i.e. in global index order.  Each rank pushes its pieces
+//      with copy-engine copies (cudaMemcpyAsync over NVLink) straight into the
+//      receivers' buffers, mapped once per buffer through CUDA IPC; a one-word
+//      ncclAllReduce then fences the exchange.  When any rank cannot map its
+//      receive buffers, every rank uses grouped ncclSend/ncclRecv instead;
 //   6. stably sort the received items on all key bits.
 // Equal keys therefore end up in global input order (stable across ranks).
 #include <cuda_runtime.h>
 #include <nccl.h>
 
 #include <algorithm>
+#include <cstddef>
+#include <cstdlib>
 #include <cstring>
+#include <map>
+#include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/cusort_b200.h"
@@ -36,6 +45,91 @@ int key_bytes(int kt) {
   }
 }
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Pinned host buffer for the gathered counts (per host thread, grown on
+// demand): a copy into pageable memory would block the host until it lands.
+struct PinnedCounts {
+  uint64_t* p = nullptr;
+  size_t cap = 0;
+  ~PinnedCounts() {
+    if (p) cudaFreeHost(p);
+  }
+  cudaError_t reserve(size_t n) {
+    if (n <= cap) return cudaSuccess;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMallocHost(reinterpret_cast<void**>(&p), n * sizeof(uint64_t));
+    if (e == cudaSuccess) cap = n;
+    return e;
+  }
+};
+thread_local PinnedCounts g_pinned_counts;
+
+// The handle behind `void* comm`: the NCCL communicator plus the receive
+// buffers of peers already mapped through CUDA IPC (opened once, closed when
+// the communicator is destroyed).
+struct MgpuComm {
+  ncclComm_t nccl = nullptr;
+  std::map<std::pair<int, std::string>, void*> mapped;  // (peer, IPC handle) -> local address
+};
+
+// Per-rank record all-gathered before the exchange.
+struct RankRecord {
+  unsigned long long counts[256];
+  cudaIpcMemHandle_t hk, hv;   // receive buffers (keys, values) of this rank
+  unsigned long long ipc_ok;   // 1 when both handles are valid
+  unsigned long long off_k, off_v;  // receive buffers' offsets inside their allocations
+  unsigned long long pad;
+};
+static_assert(sizeof(RankRecord) % 8 == 0, "record layout");
+
+// Allocation base of a device pointer (driver entry point, no link-time
+// dependency on libcuda).
+cudaError_t allocation_base(const void* p, void** base) {
+  typedef int (*GetRangeFn)(unsigned long long*, size_t*, unsigned long long);
+  static GetRangeFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f) return cudaErrorNotSupported;
+    fn = reinterpret_cast<GetRangeFn>(f);
+  }
+  unsigned long long b = 0;
+  size_t sz = 0;
+  if (fn(&b, &sz, reinterpret_cast<unsigned long long>(p)) != 0) return cudaErrorInvalidValue;
+  *base = reinterpret_cast<void*>(b);
+  return cudaSuccess;
+}
+
+// IPC handle + offset of a receive buffer; ok = false if it cannot be shared.
+bool export_buffer(const void* p, cudaIpcMemHandle_t* h, unsigned long long* off) {
+  std::memset(h, 0, sizeof(*h));
+  *off = 0;
+  if (!p) return true;  // nothing to receive into (keys-only values slot)
+  void* base = nullptr;
+  if (allocation_base(p, &base) != cudaSuccess) return false;
+  if (cudaIpcGetMemHandle(h, base) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  *off = (unsigned long long)(static_cast<const uint8_t*>(p) - static_cast<const uint8_t*>(base));
+  return true;
+}
+
+cudaError_t peer_address(MgpuComm* c, int peer, const cudaIpcMemHandle_t& h, unsigned long long off, uint8_t** out) {
+  const std::string key(reinterpret_cast<const char*>(&h), sizeof(h));
+  auto it = c->mapped.find({peer, key});
+  if (it == c->mapped.end()) {
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return e;
+    it = c->mapped.emplace(std::make_pair(peer, key), base).first;
+  }
+  *out = static_cast<uint8_t*>(it->second) + off;
+  return cudaSuccess;
+}
 
 cudaError_t nccl_to_cuda(ncclResult_t r) {
   if (r == ncclSuccess) return cudaSuccess;
@@ -77,10 +171,10 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
   }
   if (e) return e;
   size_t o = 0;
-  L->counts = o;
-  o += a256(256 * 8);
-  L->all_counts = o;
-  o += a256((size_t)nranks * 256 * 8);
+  L->counts = o;  // this rank's RankRecord (counts first), then the fence word
+  o += a256(sizeof(RankRecord) + 16);
+  L->all_counts = o;  // every rank's RankRecord
+  o += a256((size_t)nranks * sizeof(RankRecord));
   L->part_k = o;
   o += a256((size_t)n_local * kb);
   L->part_v = o;
@@ -160,13 +254,19 @@ cudaError_t cusort_mgpu_comm_init(void** comm, const unsigned char* id, int nran
   ncclComm_t c = nullptr;
   ncclResult_t r = ncclCommInitRank(&c, nranks, u, rank);
   if (r != ncclSuccess) return nccl_to_cuda(r);
-  *comm = c;
+  MgpuComm* mc = new MgpuComm();
+  mc->nccl = c;
+  *comm = mc;
   return cudaSuccess;
 }
 
 cudaError_t cusort_mgpu_comm_destroy(void* comm) {
   if (!comm) return cudaErrorInvalidValue;
-  return nccl_to_cuda(ncclCommDestroy(static_cast<ncclComm_t>(comm)));
+  MgpuComm* mc = static_cast<MgpuComm*>(comm);
+  for (auto& kv : mc->mapped) cudaIpcCloseMemHandle(kv.second);
+  const cudaError_t e = nccl_to_cuda(ncclCommDestroy(mc->nccl));
+  delete mc;
+  return e;
 }
 
 cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusort_key_type key_type,
@@ -180,7 +280,8 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   if (vb != 0 && vb != 1 && vb != 2 && vb != 4 && vb != 8 && vb != 16) return cudaErrorInvalidValue;
   if (begin_bit < 0 || end_bit < 0 || begin_bit > end_bit || end_bit > 8 * kb) return cudaErrorInvalidValue;
   if (n_local < 0 || out_capacity < 0) return cudaErrorInvalidValue;
-  ncclComm_t nc = static_cast<ncclComm_t>(comm);
+  MgpuComm* mc = static_cast<MgpuComm*>(comm);
+  ncclComm_t nc = mc->nccl;
   int nranks = 0, rank = 0;
   cudaError_t e = nccl_to_cuda(ncclCommCount(nc, &nranks));
   if (e) return e;
@@ -234,29 +335,63 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     return cudaSuccess;
   }
 
-  // 1-2. digit counts, all-gathered
+  // Receive buffers: chosen so that the final sort's last pass lands in the
+  // caller's output (pieces arrive in source-rank order).
+  const int passes = (end_bit - begin_bit + 7) / 8;
+  const bool recv_in_out = (passes % 2) == 0;
+  uint8_t* rk = static_cast<uint8_t*>(recv_in_out ? d_keys_out : (void*)(t + L.alt_k));
+  uint8_t* ok_ = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_k) : d_keys_out);
+  uint8_t* rv = static_cast<uint8_t*>(recv_in_out ? d_values_out : (void*)(t + L.alt_v));
+  uint8_t* ov = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_v) : d_values_out);
+
+  // 1-2. this rank's record (digit counts + IPC handles of its receive
+  //      buffers), all-gathered
   const int msd_begin = std::max(begin_bit, end_bit - 8);
-  unsigned long long* counts = reinterpret_cast<unsigned long long*>(t + L.counts);
-  unsigned long long* all_counts = reinterpret_cast<unsigned long long*>(t + L.all_counts);
-  e = cusort_b200::digit_counts_u64(kt, desc, d_keys_in, n_local, msd_begin, end_bit, counts, stream);
+  RankRecord* rec = reinterpret_cast<RankRecord*>(t + L.counts);
+  RankRecord* all_rec = reinterpret_cast<RankRecord*>(t + L.all_counts);
+  int* fence = reinterpret_cast<int*>(t + L.counts + sizeof(RankRecord));
+  e = cusort_b200::digit_counts_u64(kt, desc, d_keys_in, n_local, msd_begin, end_bit, rec->counts, stream);
   if (e) return e;
-  e = nccl_to_cuda(ncclAllGather(counts, all_counts, 256, ncclUint64, nc, stream));
+  const size_t tail = sizeof(RankRecord) - offsetof(RankRecord, hk);
+  e = g_pinned_counts.reserve(((size_t)nranks * sizeof(RankRecord) + tail) / 8 + 1);
   if (e) return e;
-  std::vector<uint64_t> h_all((size_t)nranks * 256);
-  e = cudaMemcpyAsync(h_all.data(), all_counts, h_all.size() * 8, cudaMemcpyDeviceToHost, stream);
+  RankRecord* h_all = reinterpret_cast<RankRecord*>(g_pinned_counts.p);
+  uint8_t* h_tail = reinterpret_cast<uint8_t*>(h_all + nranks);
+  {
+    RankRecord mine;
+    // CUSORT_MGPU_EXCHANGE=nccl forces the NCCL send/recv exchange (the flag
+    // is all-gathered, so every rank takes the same path).
+    const char* ex = std::getenv("CUSORT_MGPU_EXCHANGE");
+    const bool want_ipc = !(ex && std::strcmp(ex, "nccl") == 0);
+    const bool ok = want_ipc && export_buffer(rk, &mine.hk, &mine.off_k) &&
+                    (vb == 0 || export_buffer(rv, &mine.hv, &mine.off_v));
+    if (vb == 0) {
+      std::memset(&mine.hv, 0, sizeof(mine.hv));
+      mine.off_v = 0;
+    }
+    mine.ipc_ok = ok ? 1ull : 0ull;
+    mine.pad = 0;
+    std::memcpy(h_tail, reinterpret_cast<const uint8_t*>(&mine) + offsetof(RankRecord, hk), tail);
+  }
+  e = cudaMemcpyAsync(reinterpret_cast<uint8_t*>(rec) + offsetof(RankRecord, hk), h_tail, tail,
+                      cudaMemcpyHostToDevice, stream);
   if (e) return e;
-  e = cudaStreamSynchronize(stream);
+  e = nccl_to_cuda(ncclAllGather(rec, all_rec, sizeof(RankRecord), ncclUint8, nc, stream));
   if (e) return e;
+  e = cudaMemcpyAsync(h_all, all_rec, (size_t)nranks * sizeof(RankRecord), cudaMemcpyDeviceToHost, stream);
+  if (e) return e;
+  cudaEvent_t counts_ready;
+  e = cudaEventCreateWithFlags(&counts_ready, cudaEventDisableTiming);
+  if (e) return e;
+  e = cudaEventRecord(counts_ready, stream);
+  if (e) {
+    cudaEventDestroy(counts_ready);
+    return e;
+  }
 
-  // 3. plan (identical on every rank)
-  std::vector<int64_t> send((size_t)nranks), recv((size_t)nranks), totals((size_t)nranks);
-  if (cusort_mgpu_plan(h_all.data(), nranks, rank, nullptr, send.data(), recv.data(), totals.data()))
-    return cudaErrorInvalidValue;
-  for (int q = 0; q < nranks; ++q)
-    if (totals[q] > out_capacity) return cudaErrorInvalidValue;  // every rank sees it: no rank enters NCCL
-  const int64_t n_recv = totals[rank];
-
-  // 4. stable partition by the owner digit
+  // 4. stable partition by the owner digit -- enqueued before the host waits
+  //    for the records, so the host round trip overlaps this pass.  (It does
+  //    not depend on the plan: owners are contiguous digit ranges.)
   void* part_k = t + L.part_k;
   void* part_v = t + L.part_v;
   if (vb)
@@ -268,17 +403,66 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     e = desc ? cusort_sort_keys_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin,
                                            end_bit, stream)
              : cusort_sort_keys(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin, end_bit, stream);
-  if (e) return e;
+  if (e) {
+    cudaEventDestroy(counts_ready);
+    return e;
+  }
 
-  // 5. all-to-all: received pieces in source-rank order.  The receive buffer is
-  //    chosen so that the final sort's last pass lands in the caller's output.
-  const int passes = (end_bit - begin_bit + 7) / 8;
-  const bool recv_in_out = (passes % 2) == 0;
-  uint8_t* rk = static_cast<uint8_t*>(recv_in_out ? d_keys_out : (void*)(t + L.alt_k));
-  uint8_t* ok_ = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_k) : d_keys_out);
-  uint8_t* rv = static_cast<uint8_t*>(recv_in_out ? d_values_out : (void*)(t + L.alt_v));
-  uint8_t* ov = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_v) : d_values_out);
-  {
+  // 3. plan (identical on every rank)
+  e = cudaEventSynchronize(counts_ready);
+  cudaEventDestroy(counts_ready);
+  if (e) return e;
+  std::vector<uint64_t> all_counts((size_t)nranks * 256);
+  bool all_ipc = true;
+  for (int q = 0; q < nranks; ++q) {
+    std::memcpy(&all_counts[(size_t)q * 256], h_all[q].counts, 256 * 8);
+    all_ipc = all_ipc && h_all[q].ipc_ok == 1ull;
+  }
+  std::vector<int64_t> send((size_t)nranks), recv((size_t)nranks), totals((size_t)nranks);
+  if (cusort_mgpu_plan(all_counts.data(), nranks, rank, nullptr, send.data(), recv.data(), totals.data()))
+    return cudaErrorInvalidValue;
+  for (int q = 0; q < nranks; ++q)
+    if (totals[q] > out_capacity) return cudaErrorInvalidValue;  // every rank sees it: no rank enters NCCL
+  const int64_t n_recv = totals[rank];
+
+  // 5. all-to-all
+  if (all_ipc) {
+    // Push this rank's piece for q into q's receive buffers at the offset of
+    // source `rank` (the pieces of lower ranks come first).
+    std::vector<int> owner(256);
+    if (cusort_mgpu_plan(all_counts.data(), nranks, rank, owner.data(), nullptr, nullptr, nullptr))
+      return cudaErrorInvalidValue;
+    int64_t so = 0;
+    for (int q = 0; q < nranks && !e; ++q) {
+      if (send[q] > 0) {
+        int64_t at = 0;  // items q receives from the ranks below this one
+        for (int p = 0; p < rank; ++p)
+          for (int d = 0; d < 256; ++d)
+            if (owner[d] == q) at += (int64_t)all_counts[(size_t)p * 256 + d];
+        uint8_t* dk = nullptr;
+        uint8_t* dv = nullptr;
+        if (q == rank) {
+          dk = rk;
+          dv = rv;
+        } else {
+          e = peer_address(mc, q, h_all[q].hk, h_all[q].off_k, &dk);
+          if (!e && vb) e = peer_address(mc, q, h_all[q].hv, h_all[q].off_v, &dv);
+        }
+        if (!e)
+          e = cudaMemcpyAsync(dk + at * kb, static_cast<uint8_t*>(part_k) + so * kb, (size_t)send[q] * kb,
+                              cudaMemcpyDeviceToDevice, stream);
+        if (!e && vb)
+          e = cudaMemcpyAsync(dv + at * vb, static_cast<uint8_t*>(part_v) + so * vb, (size_t)send[q] * vb,
+                              cudaMemcpyDeviceToDevice, stream);
+      }
+      so += send[q];
+    }
+    // Fence: once every rank's copies (earlier on its stream) are done, the
+    // all-reduce completes everywhere and the received data is complete.
+    if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
+    if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
+    if (e) return e;
+  } else {
     ncclResult_t r = ncclGroupStart();
     int64_t so = 0, ro = 0;
     for (int q = 0; q < nranks && r == ncclSuccess; ++q) {

@@ -44,6 +44,7 @@ def run(args, torch):
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     sorter = None
     try:
