@@ -141,7 +141,7 @@ def run(args, torch):
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "int32 keys / uint32 values (integer radix)",
             "data": "synthetic (seeded uniform int32 keys per rank, values = global index)",
-            "config": {"workload": "configs[4]-style sharded global sort, MSD all-gather + NCCL all-to-all + local sort",
+            "config": {"workload": "configs[4]-style sharded global sort: MSD-digit all-gather, partition pass, all-to-all (copy-engine pushes over NVLink into IPC-mapped peer buffers), local sort",
                        "n_total": n_total, "n_per_gpu": n_local, "parallelism": f"shard{world}",
                        "l2": "inputs per GPU 512 MiB > L2"},
             "verified": {"ranks_sorted": sorted_ok, "ranks_ordered": order_ok, "counts": counts_ok},
