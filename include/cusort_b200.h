@@ -163,9 +163,16 @@ cudaError_t cusort_sort_db_noalloc(cusort_key_type key_type, cusort_double_buffe
  * back a contiguous part of the globally sorted sequence (ranks' outputs
  * concatenated in rank order are the global result), stable by global index.
  * Steps: most-significant-digit counts, ncclAllGather of G x 256 counts, a
- * digit -> owner plan computed identically on every rank, a stable local
- * partition pass, a grouped ncclSend/ncclRecv all-to-all of keys and values,
- * and a stable local sort of the received items.
+ * digit -> owner plan computed identically on every rank, one stable
+ * partition pass whose stores go straight into the owning ranks' output
+ * buffers over NVLink (peer memory mapped through CUDA IPC; fenced by a
+ * one-word ncclAllReduce), and a stable local sort of the received items.
+ * Environment CUSORT_MGPU_EXCHANGE=copy|nccl (or a rank whose buffers cannot
+ * be mapped) selects a local partition pass followed by copy-engine pushes
+ * or grouped ncclSend/ncclRecv instead.  The output buffers are written by
+ * other ranks' kernels: they must be device allocations (cudaMalloc or a
+ * caching allocator over it) and must not be used from other streams while a
+ * call runs.
  *
  * cusort_mgpu_unique_id: on one rank; the caller broadcasts the 128 bytes.
  * cusort_mgpu_comm_init: every rank, with its GPU current.
@@ -203,7 +210,8 @@ int cusort_set_launch_mode(int mode);
 
 /* Device status word of the last sort that used this temp storage:
  * 0 = ok, bit 0 = a lookback wait timed out, bit 1 = a tile-copy wait timed
- * out.  Synchronises `stream`. */
+ * out, bit 2 = (cusort_mgpu_sort temp storage) a partition store fell outside
+ * its destination buffer and was skipped.  Synchronises `stream`. */
 cudaError_t cusort_read_device_status(const void* d_temp_storage, uint32_t* status, cudaStream_t stream);
 
 /* Bound on every device-side wait, in nanoseconds (default 2e9).  Per host

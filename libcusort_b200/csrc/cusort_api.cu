@@ -565,6 +565,83 @@ cudaError_t digit_counts_u64(int kt, bool desc, const void* keys, int64_t n, int
   return cudaLaunchKernelExC(&cfg, p.hist.func, args);
 }
 
+cudaError_t routed_partition(int kt, size_t vb, bool desc, const void* keys, const void* vals, int64_t n,
+                             int begin_bit, int end_bit, bool wide_offsets, const RouteTable* d_route, void* d_temp,
+                             size_t* temp_bytes, cudaStream_t stream) {
+  const int kb = key_bytes_of(kt);
+  if (kb == 0 || temp_bytes == nullptr || n < 0) return cudaErrorInvalidValue;
+  if (vb != 0 && !value_bytes_ok(vb)) return cudaErrorInvalidValue;
+  if (begin_bit < 0 || end_bit <= begin_bit || end_bit - begin_bit > kRadixBits || end_bit > 8 * kb)
+    return cudaErrorInvalidValue;
+  const int offb = (wide_offsets || (uint64_t)n >= (1ull << 30)) ? 8 : 4;
+  const bool fk = (kt == CUSORT_KEY_F32 || kt == CUSORT_KEY_F64);
+  KernelInfo os;
+  bool ok = false;
+  switch (kb) {
+    case 1: case 2: ok = get_routed_k12(kb, (int)vb, offb, fk, &os); break;
+    case 4: ok = get_routed_k4((int)vb, offb, fk, &os); break;
+    case 8: ok = get_routed_k8((int)vb, offb, fk, &os); break;
+    default: ok = false;
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  const uint64_t tiles = ((uint64_t)n + os.tile - 1) / os.tile;
+  const size_t need = kCtrlBytes + align256((size_t)std::max<uint64_t>(tiles, 1) * kRadix * offb);
+  if (d_temp == nullptr) {
+    *temp_bytes = need;
+    return cudaSuccess;
+  }
+  if (*temp_bytes < need || d_route == nullptr || (reinterpret_cast<uintptr_t>(d_temp) & 15) != 0)
+    return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+
+  int dev = 0, sms = 0, occ = 0;
+  CUSORT_TRY(cudaGetDevice(&dev));
+  CUSORT_TRY(get_sm_count(dev, &sms));
+  CUSORT_TRY(get_occupancy(dev, os, &occ));
+  uint8_t* t = static_cast<uint8_t*>(d_temp);
+  std::vector<Launch> ls(2);
+  Launch& li = ls[0];
+  li = Launch{};
+  li.func = get_init_kernel();
+  const uint64_t n16 = need / 16;
+  li.grid = (int)std::min<uint64_t>((uint64_t)sms * 4, std::max<uint64_t>(1, (n16 + 511) / 512));
+  li.threads = 512;
+  li.pdl = false;
+  li.kind = 0;
+  li.args.init.ptr = d_temp;
+  li.args.init.n16 = n16;
+  Launch& l = ls[1];
+  l = Launch{};
+  l.func = os.func;
+  l.grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ, tiles));
+  l.threads = os.threads;
+  l.smem = os.smem;
+  l.pdl = true;
+  l.kind = 2;
+  OnesweepArgs& a = l.args.os;
+  uint64_t tw_c = 0, tw_f = 0;
+  twiddle_constants(kt, kb, desc, &tw_c, &tw_f);
+  a.keys_in = keys;
+  a.vals_in = vb ? vals : nullptr;
+  a.n = (uint64_t)n;
+  a.tw_c = tw_c;
+  a.tw_f = tw_f;
+  a.shift = (uint32_t)begin_bit;
+  a.mask = (1u << (end_bit - begin_bit)) - 1u;
+  a.pass = 0;
+  a.num_tiles = (uint32_t)tiles;
+  a.desc = t + kCtrlBytes;
+  a.tile_counter = reinterpret_cast<uint32_t*>(t + 64);
+  a.status = reinterpret_cast<uint32_t*>(t);
+  a.spin_limit_ns = g_ts.wait_limit_ns;
+  a.skip_tile = g_ts.skip_tile;
+  const size_t tile_k = (size_t)os.tile * kb, tile_v = (size_t)os.tile * vb;
+  a.tma_keys = ((reinterpret_cast<uintptr_t>(keys) & 15) == 0 && (tile_k & 15) == 0) ? 1u : 0u;
+  a.tma_vals = (vb == 0 || ((reinterpret_cast<uintptr_t>(vals) & 15) == 0 && (tile_v & 15) == 0)) ? 1u : 0u;
+  a.g_hist_pass = d_route;  // routed kernels read their RouteTable here
+  return launch_direct(ls, stream);
+}
+
 // DoubleBuffer sort whose temp storage is a caller-provided scratch region
 // of `scratch_bytes` (used by the no-allocation entry point): rejects calls
 // whose temp storage would not fit, and always launches directly.

@@ -254,10 +254,11 @@ __device__ __forceinline__ uint32_t atom_add_shared_if(uint32_t pred, uint32_t* 
 }
 
 // Inclusive warp scan (shfl_up) of 32-bit values.
-__device__ __forceinline__ uint32_t warp_inclusive_scan(uint32_t v, uint32_t lane) {
+template <typename T>
+__device__ __forceinline__ T warp_inclusive_scan(T v, uint32_t lane) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+    T t = __shfl_up_sync(0xffffffffu, v, o);
     if (lane >= (uint32_t)o) v += t;
   }
   return v;

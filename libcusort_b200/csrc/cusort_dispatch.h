@@ -23,6 +23,10 @@ bool get_kernels_k1(int value_bytes, int off_bytes, bool float_key, KernelInfo* 
 bool get_kernels_k2(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 bool get_kernels_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 bool get_kernels_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
+// Routed onesweep kernels (kernels_routed_*.cu): the multi-GPU partition pass.
+bool get_routed_k12(int key_bytes, int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
+bool get_routed_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
+bool get_routed_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
 const void* get_init_kernel();
 // Count-and-fill kernel of 1-byte keys-only full-range sorts (kernels_k1.cu).
 const void* get_fill_bytes_kernel(int off_bytes);
@@ -35,5 +39,16 @@ cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type
 // Single-digit counts (u64[256]) of the twiddled keys (cusort_api.cu).
 cudaError_t digit_counts_u64(int key_type, bool descending, const void* keys, int64_t num_items, int begin_bit,
                              int end_bit, unsigned long long* d_counts, cudaStream_t stream);
+
+struct RouteTable;
+// One stable partition pass over the digit [begin_bit, end_bit) (at most 8
+// bits) whose write-out goes straight to route->kptr/vptr[owner[d]] at
+// route->base[d] + (rank of the item among this call's items of digit d):
+// the fused partition + exchange of the multi-GPU sort.  `d_route` is device
+// memory.  wide_offsets selects 64-bit offsets (destinations >= 2^32 items).
+// With d_temp == nullptr only *temp_bytes is set (cusort_api.cu).
+cudaError_t routed_partition(int key_type, size_t value_bytes, bool descending, const void* keys, const void* values,
+                             int64_t num_items, int begin_bit, int end_bit, bool wide_offsets,
+                             const RouteTable* d_route, void* d_temp, size_t* temp_bytes, cudaStream_t stream);
 
 }  // namespace cusort_b200

@@ -52,10 +52,10 @@ struct TileShape {
 constexpr int kHistThreads = 1024;
 constexpr int kHistUnroll = 4;
 
-template <int KB, int VB, typename Off, bool FK>
+template <int KB, int VB, typename Off, bool FK, bool ROUTED = false>
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB>;
-  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK>;
+  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED>;
   os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;
   os->tile = CFG::TILE;
@@ -70,15 +70,15 @@ inline void fill_histogram(KernelInfo* h) {
   h->smem = HistShape<KB>::SMEM;
 }
 
-template <int KB, typename Off, bool FK>
+template <int KB, typename Off, bool FK, bool ROUTED = false>
 inline bool fill_for_value(int vb, KernelInfo* os) {
   switch (vb) {
-    case 0: fill_onesweep<KB, 0, Off, FK>(os); return true;
-    case 1: fill_onesweep<KB, 1, Off, FK>(os); return true;
-    case 2: fill_onesweep<KB, 2, Off, FK>(os); return true;
-    case 4: fill_onesweep<KB, 4, Off, FK>(os); return true;
-    case 8: fill_onesweep<KB, 8, Off, FK>(os); return true;
-    case 16: fill_onesweep<KB, 16, Off, FK>(os); return true;
+    case 0: fill_onesweep<KB, 0, Off, FK, ROUTED>(os); return true;
+    case 1: fill_onesweep<KB, 1, Off, FK, ROUTED>(os); return true;
+    case 2: fill_onesweep<KB, 2, Off, FK, ROUTED>(os); return true;
+    case 4: fill_onesweep<KB, 4, Off, FK, ROUTED>(os); return true;
+    case 8: fill_onesweep<KB, 8, Off, FK, ROUTED>(os); return true;
+    case 16: fill_onesweep<KB, 16, Off, FK, ROUTED>(os); return true;
     default: return false;
   }
 }
@@ -105,6 +105,23 @@ inline bool get_kernels_impl(int vb, int offb, bool float_key, KernelInfo* os, K
     if (float_key) return false;
   }
   return get_kernels_fk<KB, false>(vb, offb, os, h);
+}
+
+// Routed onesweep kernels (single partition pass of the multi-GPU sort).
+template <int KB>
+inline bool get_routed_impl(int vb, int offb, bool float_key, KernelInfo* os) {
+  if constexpr (KB == 4 || KB == 8) {
+    if (float_key) {
+      if (offb == 4) return fill_for_value<KB, unsigned int, true, true>(vb, os);
+      if (offb == 8) return fill_for_value<KB, unsigned long long, true, true>(vb, os);
+      return false;
+    }
+  } else {
+    if (float_key) return false;
+  }
+  if (offb == 4) return fill_for_value<KB, unsigned int, false, true>(vb, os);
+  if (offb == 8) return fill_for_value<KB, unsigned long long, false, true>(vb, os);
+  return false;
 }
 
 }  // namespace cusort_b200

@@ -451,10 +451,13 @@ struct RankSlots {
 #define CUSORT_RANK_MODE_OF(KB, VB) \
   (CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE : (((VB) == 0 && (KB) <= 4) ? CUSORT_KEYS_RANK_MODE : 4))
 
-template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_>
+template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_, bool ROUTED_ = false>
 struct OnesweepCfg {
   static constexpr int KB = KB_, VB = VB_, THREADS = THREADS_, KPT = KPT_, MINB = MINB_;
   static constexpr bool FLOAT_KEY = FLOAT_KEY_;
+  // Routed pass (multi-GPU partition): digit bases and destinations come from
+  // a RouteTable, stores may target peers' memory.
+  static constexpr bool ROUTED = ROUTED_;
   // Measured on B200 (2^26 items): mode 4 is fastest for pairs and 8-byte
   // keys; for keys-only <= 4 bytes its extra registers spill and mode 3 wins.
   static constexpr int RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
@@ -490,7 +493,18 @@ struct OnesweepCfg {
   static constexpr size_t OFF_GOFF = OFF_GBASE + kRadix * sizeof(Off);
   static constexpr size_t OFF_MISC = OFF_GOFF + kRadix * sizeof(Off);
   static constexpr size_t OFF_MBAR = OFF_MISC + 16 * 4;
-  static constexpr size_t SMEM_BYTES = OFF_MBAR + 2 * 8;
+  // routed: owner[256] (u8); kptr/vptr/cap/base[kMaxRouteRanks] (u64); the
+  // tile's digit prefix of earlier tiles' counts pre[256] + 8 warp totals
+  // (u64); each owner's first and last digit [2][kMaxRouteRanks] (u32); per
+  // digit the tile's destination addresses dk/dv[256] (u64)
+  static constexpr size_t OFF_ROUTE = OFF_MBAR + 2 * 8;
+  static constexpr size_t OFF_RPTR = OFF_ROUTE + kRadix;
+  static constexpr size_t OFF_RPRE = OFF_RPTR + 4 * 8 * kMaxRouteRanks;
+  static constexpr size_t OFF_RFIRST = OFF_RPRE + 8 * (kRadix + 8);
+  static constexpr size_t OFF_RDST = OFF_RFIRST + 2 * 4 * kMaxRouteRanks;
+  static constexpr size_t ROUTE_BYTES = ROUTED ? (OFF_RDST + 2 * 8 * kRadix - OFF_ROUTE) : 0;
+  static_assert(!(ROUTED && PREFETCH), "routed passes take tickets one tile at a time");
+  static constexpr size_t SMEM_BYTES = OFF_ROUTE + ROUTE_BYTES;
   static_assert(THREADS >= kRadix && THREADS % 32 == 0, "need >= 256 threads");
   static_assert(TILE * (KB + VB) < (1 << 20), "mbarrier tx-count limit");
   static_assert(32 * KPT < (1 << 24), "rank packing");
@@ -614,7 +628,25 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 
   // Global exclusive offset of every digit for this pass (from the upfront
   // histogram), computed once per CTA; the first tile ticket is taken here.
-  {
+  if constexpr (CFG::ROUTED) {
+    // Destinations: owner of each digit; per owner its buffers, capacity,
+    // this rank's offset in it and its first digit.
+    unsigned char* s_owner = smem + CFG::OFF_ROUTE;
+    unsigned long long* s_rptr = reinterpret_cast<unsigned long long*>(smem + CFG::OFF_RPTR);
+    uint32_t* s_rfirst = reinterpret_cast<uint32_t*>(smem + CFG::OFF_RFIRST);
+    const RouteTable* route = static_cast<const RouteTable*>(a.g_hist_pass);
+    if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
+    if (tid < kRadix) s_owner[tid] = route->owner[tid];
+    if (tid < kMaxRouteRanks) {
+      s_rptr[tid] = route->kptr[tid];
+      s_rptr[kMaxRouteRanks + tid] = route->vptr[tid];
+      s_rptr[2 * kMaxRouteRanks + tid] = route->cap[tid];
+      s_rptr[3 * kMaxRouteRanks + tid] = route->base[tid];
+      s_rfirst[tid] = route->first_digit[tid];
+      s_rfirst[kMaxRouteRanks + tid] = route->last_digit[tid];
+    }
+    __syncthreads();
+  } else {
     if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
     Off cv = (tid < kRadix) ? static_cast<const Off*>(a.g_hist_pass)[tid] : Off(0);
     Off incl = cv;
@@ -827,14 +859,78 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         if (publish)
           dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
       }
-      s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+      if constexpr (CFG::ROUTED) {
+        // Inclusive prefix over digits of the earlier tiles' counts (warp
+        // part here, warp totals added after the barrier): the items of an
+        // owner in earlier tiles are a difference of two prefixes.
+        unsigned long long* s_pre = reinterpret_cast<unsigned long long*>(smem + CFG::OFF_RPRE);
+        const unsigned long long incl_x = dev::warp_inclusive_scan<unsigned long long>(excl, lane);
+        s_pre[tid] = incl_x;
+        if (lane == 31) s_pre[kRadix + warp] = incl_x;
+      } else {
+        s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+      }
     }
     reorder();
     __syncthreads();
+    if constexpr (CFG::ROUTED) {
+      // Owner q receives, per source rank, that rank's tiles in order, each
+      // tile's items of q in the tile's (digit-sorted) order: one contiguous
+      // run per (tile, owner).  Resolve each digit's address once (dst(j) =
+      // addr + j for tile position j); a run that would not fit is dropped
+      // and flagged.
+      if (tid < kRadix) {
+        const unsigned long long* s_rptr = reinterpret_cast<const unsigned long long*>(smem + CFG::OFF_RPTR);
+        const unsigned long long* s_pre = reinterpret_cast<const unsigned long long*>(smem + CFG::OFF_RPRE);
+        const uint32_t* s_rfirst = reinterpret_cast<const uint32_t*>(smem + CFG::OFF_RFIRST);
+        unsigned long long* s_dst = reinterpret_cast<unsigned long long*>(smem + CFG::OFF_RDST);
+        const uint32_t q = smem[CFG::OFF_ROUTE + tid];
+        const uint32_t lo = s_rfirst[q], hi = s_rfirst[kMaxRouteRanks + q];  // owner's digits [lo, hi]
+        // inclusive digit prefix at x (over all 8 warps' parts)
+        auto prefix = [&](uint32_t x) {
+          unsigned long long v = s_pre[x];
+          for (uint32_t w = 0; w < (x >> 5); ++w) v += s_pre[kRadix + w];
+          return v;
+        };
+        const unsigned long long earlier = prefix(hi) - (lo ? prefix(lo - 1) : 0ull);
+        // position of the owner's run in its buffer, and of this digit in it
+        const unsigned long long run = s_rptr[3 * kMaxRouteRanks + q] + earlier;
+        const unsigned long long rel = run - (unsigned long long)s_tstart[lo];  // modulo 2^64
+        const unsigned long long first = rel + s_tstart[tid];
+        unsigned long long dk = 0, dv = 0;
+        if (first + cnt <= s_rptr[2 * kMaxRouteRanks + q]) {
+          dk = s_rptr[q] + rel * sizeof(K);
+          if constexpr (HAS_V) dv = s_rptr[kMaxRouteRanks + q] + rel * sizeof(V);
+        } else if (cnt) {
+          atomicOr(a.status, kStatusRouteOverflow);
+        }
+        s_dst[tid] = dk;
+        s_dst[kRadix + tid] = dv;
+      }
+      __syncthreads();
+    }
 
     // ---- 6. coalesced scatter
     auto put_one = [&](uint32_t j) {
-      if constexpr (CFG::PACKED_KV) {
+      if constexpr (CFG::ROUTED) {
+        K k;
+        V v;
+        if constexpr (CFG::PACKED_KV) {
+          const uint2 kv = s_kv[j];
+          k = (K)kv.x;
+          v = (V)kv.y;
+        } else {
+          k = s_keys[j];
+          if constexpr (HAS_V) v = s_vals[j];
+        }
+        const unsigned long long* s_dst = reinterpret_cast<const unsigned long long*>(smem + CFG::OFF_RDST);
+        const uint32_t d = dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
+        const unsigned long long dk = s_dst[d];
+        if (dk != 0ull) {  // 0: the run did not fit (flagged above)
+          reinterpret_cast<K*>(dk)[j] = k;
+          if constexpr (HAS_V) reinterpret_cast<V*>(s_dst[kRadix + d])[j] = v;
+        }
+      } else if constexpr (CFG::PACKED_KV) {
         const uint2 kv = s_kv[j];
         const K k = (K)kv.x;
         const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
@@ -859,6 +955,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       if (NBUF == 2) b ^= 1;
     }
   }
+  if constexpr (CFG::ROUTED) __threadfence_system();  // peer stores visible before the kernel ends
 }
 
 }  // namespace cusort_b200

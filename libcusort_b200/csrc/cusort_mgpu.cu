@@ -9,20 +9,26 @@
 //      (cusort_mgpu_plan): digits go to ranks in order, each by the midpoint
 //      of its share of the global count, so rank q owns a contiguous digit
 //      range and the ranks' outputs concatenate to the global order;
-//   4. stably partition the local slice by that digit (one onesweep pass);
-//   5. exchange keys and values, all-to-all; the receiver lays the pieces out
-//      by source rank, i.e. in global index order.  Each rank pushes its pieces
-//      with copy-engine copies (cudaMemcpyAsync over NVLink) straight into the
-//      receivers' buffers, mapped once per buffer through CUDA IPC; a one-word
-//      ncclAllReduce then fences the exchange.  When any rank cannot map its
-//      receive buffers, every rank uses grouped ncclSend/ncclRecv instead;
+//   4+5. partition the local slice by that digit and exchange it, all-to-all.
+//      Default ("routed"): ONE onesweep pass over the digit whose write-out
+//      stores, per tile and owner, the tile's (digit-sorted) items of that
+//      owner as one contiguous run straight into the owner's receive buffer
+//      over NVLink (peer buffers mapped once through CUDA IPC), tiles in
+//      order after the runs of lower source ranks.  Long runs keep the
+//      remote stores efficient.  A one-word ncclAllReduce then fences the
+//      exchange.  Fallbacks, chosen when a rank cannot map its buffers (or by
+//      CUSORT_MGPU_EXCHANGE=copy|nccl): a local partition pass, then
+//      copy-engine pushes into the mapped peer buffers ("copy") or grouped
+//      ncclSend/ncclRecv ("nccl"), pieces laid out by source rank;
 //   6. stably sort the received items on all key bits.
-// Equal keys therefore end up in global input order (stable across ranks).
+// In every layout, equal keys (which share the digit) arrive in global input
+// order, so they end up in global input order (stable across ranks).
 #include <cuda_runtime.h>
 #include <nccl.h>
 
 #include <algorithm>
 #include <cstddef>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -32,6 +38,7 @@
 
 #include "../../include/cusort_b200.h"
 #include "cusort_dispatch.h"
+#include "cusort_types.h"
 
 namespace {
 
@@ -74,13 +81,16 @@ struct MgpuComm {
   std::map<std::pair<int, std::string>, void*> mapped;  // (peer, IPC handle) -> local address
 };
 
+// Exchange modes, ordered: the call uses the lowest mode any rank asks for.
+enum : unsigned long long { kXchgNccl = 0, kXchgCopy = 1, kXchgRouted = 2 };
+
 // Per-rank record all-gathered before the exchange.
 struct RankRecord {
   unsigned long long counts[256];
   cudaIpcMemHandle_t hk, hv;   // receive buffers (keys, values) of this rank
-  unsigned long long ipc_ok;   // 1 when both handles are valid
+  unsigned long long mode;     // kXchg*: highest exchange mode this rank supports
   unsigned long long off_k, off_v;  // receive buffers' offsets inside their allocations
-  unsigned long long pad;
+  unsigned long long cap;      // receive capacity (items) of this rank
 };
 static_assert(sizeof(RankRecord) % 8 == 0, "record layout");
 
@@ -131,6 +141,41 @@ cudaError_t peer_address(MgpuComm* c, int peer, const cudaIpcMemHandle_t& h, uns
   return cudaSuccess;
 }
 
+// Phase timing of one call (environment CUSORT_MGPU_TIMING=1): events on the
+// stream at each phase boundary, printed to stderr when the call returns.
+struct PhaseTimer {
+  static constexpr int kMax = 8;
+  bool on = false;
+  cudaStream_t stream = nullptr;
+  int n = 0, rank = 0;
+  cudaEvent_t ev[kMax];
+  const char* name[kMax];
+  PhaseTimer(cudaStream_t s, int r) : stream(s), rank(r) {
+    const char* v = std::getenv("CUSORT_MGPU_TIMING");
+    on = v && v[0] == '1';
+  }
+  void mark(const char* what) {
+    if (!on || n >= kMax) return;
+    if (cudaEventCreate(&ev[n]) != cudaSuccess) return;
+    name[n] = what;
+    cudaEventRecord(ev[n], stream);
+    ++n;
+  }
+  ~PhaseTimer() {
+    if (!on || n == 0) return;
+    if (cudaEventSynchronize(ev[n - 1]) == cudaSuccess) {
+      std::fprintf(stderr, "cusort_mgpu rank %d:", rank);
+      for (int i = 1; i < n; ++i) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, ev[i - 1], ev[i]);
+        std::fprintf(stderr, " %s %.3f", name[i], ms);
+      }
+      std::fprintf(stderr, " (ms)\n");
+    }
+    for (int i = 0; i < n; ++i) cudaEventDestroy(ev[i]);
+  }
+};
+
 cudaError_t nccl_to_cuda(ncclResult_t r) {
   if (r == ncclSuccess) return cudaSuccess;
   if (r == ncclInvalidArgument || r == ncclInvalidUsage) return cudaErrorInvalidValue;
@@ -138,7 +183,8 @@ cudaError_t nccl_to_cuda(ncclResult_t r) {
 }
 
 struct MgpuLayout {
-  size_t counts, all_counts, part_k, part_v, alt_k, alt_v, sort_tmp, sort_tmp_bytes, total;
+  size_t route_tmp, route_tmp_bytes, route, counts, all_counts, part_k, part_v, alt_k, alt_v, sort_tmp,
+      sort_tmp_bytes, total;
 };
 
 // Temp storage of one call; the local sorts' sizes come from this library's
@@ -170,7 +216,16 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
     e = cusort_sort_keys(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, begin, end, nullptr);
   }
   if (e) return e;
+  size_t route_tmp = 0;
+  e = cusort_b200::routed_partition(kt, vb, desc, nullptr, nullptr, n_local, msd_begin, end, true, nullptr, nullptr,
+                                    &route_tmp, nullptr);
+  if (e) return e;
   size_t o = 0;
+  L->route_tmp = o;  // first, so that the status word at d_temp is the routed pass's
+  L->route_tmp_bytes = route_tmp;
+  o += a256(route_tmp);
+  L->route = o;
+  o += a256(sizeof(cusort_b200::RouteTable));
   L->counts = o;  // this rank's RankRecord (counts first), then the fence word
   o += a256(sizeof(RankRecord) + 16);
   L->all_counts = o;  // every rank's RankRecord
@@ -313,7 +368,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     *temp_bytes = L.total;
     return cudaSuccess;
   }
-  if (*temp_bytes < L.total) return cudaErrorInvalidValue;
+  if (*temp_bytes < L.total || (reinterpret_cast<uintptr_t>(d_temp) & 15) != 0) return cudaErrorInvalidValue;
   uint8_t* t = static_cast<uint8_t*>(d_temp);
   void* stmp = t + L.sort_tmp;
   size_t stmp_bytes = L.sort_tmp_bytes;
@@ -344,9 +399,11 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   uint8_t* rv = static_cast<uint8_t*>(recv_in_out ? d_values_out : (void*)(t + L.alt_v));
   uint8_t* ov = static_cast<uint8_t*>(recv_in_out ? (void*)(t + L.alt_v) : d_values_out);
 
-  // 1-2. this rank's record (digit counts + IPC handles of its receive
-  //      buffers), all-gathered
+  // 1-2. this rank's record (digit counts, receive capacity, exchange mode,
+  //      IPC handles of its receive buffers), all-gathered
   const int msd_begin = std::max(begin_bit, end_bit - 8);
+  PhaseTimer timer(stream, rank);
+  timer.mark("start");
   RankRecord* rec = reinterpret_cast<RankRecord*>(t + L.counts);
   RankRecord* all_rec = reinterpret_cast<RankRecord*>(t + L.all_counts);
   int* fence = reinterpret_cast<int*>(t + L.counts + sizeof(RankRecord));
@@ -357,20 +414,25 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   if (e) return e;
   RankRecord* h_all = reinterpret_cast<RankRecord*>(g_pinned_counts.p);
   uint8_t* h_tail = reinterpret_cast<uint8_t*>(h_all + nranks);
+  unsigned long long my_mode = kXchgNccl;
   {
     RankRecord mine;
-    // CUSORT_MGPU_EXCHANGE=nccl forces the NCCL send/recv exchange (the flag
-    // is all-gathered, so every rank takes the same path).
+    // CUSORT_MGPU_EXCHANGE=copy|nccl selects a fallback exchange (the mode is
+    // all-gathered, so every rank takes the same path).
     const char* ex = std::getenv("CUSORT_MGPU_EXCHANGE");
-    const bool want_ipc = !(ex && std::strcmp(ex, "nccl") == 0);
-    const bool ok = want_ipc && export_buffer(rk, &mine.hk, &mine.off_k) &&
+    unsigned long long want = kXchgRouted;
+    if (ex && std::strcmp(ex, "nccl") == 0) want = kXchgNccl;
+    if (ex && std::strcmp(ex, "copy") == 0) want = kXchgCopy;
+    if (want == kXchgRouted && nranks > cusort_b200::kMaxRouteRanks) want = kXchgCopy;
+    const bool ok = want != kXchgNccl && export_buffer(rk, &mine.hk, &mine.off_k) &&
                     (vb == 0 || export_buffer(rv, &mine.hv, &mine.off_v));
     if (vb == 0) {
       std::memset(&mine.hv, 0, sizeof(mine.hv));
       mine.off_v = 0;
     }
-    mine.ipc_ok = ok ? 1ull : 0ull;
-    mine.pad = 0;
+    my_mode = ok ? want : kXchgNccl;
+    mine.mode = my_mode;
+    mine.cap = (unsigned long long)out_capacity;
     std::memcpy(h_tail, reinterpret_cast<const uint8_t*>(&mine) + offsetof(RankRecord, hk), tail);
   }
   e = cudaMemcpyAsync(reinterpret_cast<uint8_t*>(rec) + offsetof(RankRecord, hk), h_tail, tail,
@@ -388,24 +450,34 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     cudaEventDestroy(counts_ready);
     return e;
   }
+  timer.mark("counts+gather");
 
-  // 4. stable partition by the owner digit -- enqueued before the host waits
-  //    for the records, so the host round trip overlaps this pass.  (It does
-  //    not depend on the plan: owners are contiguous digit ranges.)
+  // 4 (fallback modes). stable partition by the owner digit into part_k/v.
+  //    Unless this rank asked for the routed exchange, it is enqueued before
+  //    the host waits for the records, so the host round trip overlaps this
+  //    pass.  (It does not depend on the plan: owners are contiguous digit
+  //    ranges.)
   void* part_k = t + L.part_k;
   void* part_v = t + L.part_v;
-  if (vb)
-    e = desc ? cusort_sort_pairs_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, vb, d_values_in, part_v,
-                                            n_local, msd_begin, end_bit, stream)
-             : cusort_sort_pairs(stmp, &stmp_bytes, key_type, d_keys_in, part_k, vb, d_values_in, part_v, n_local,
-                                 msd_begin, end_bit, stream);
-  else
-    e = desc ? cusort_sort_keys_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin,
-                                           end_bit, stream)
-             : cusort_sort_keys(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin, end_bit, stream);
-  if (e) {
-    cudaEventDestroy(counts_ready);
-    return e;
+  auto partition = [&]() -> cudaError_t {
+    if (vb)
+      return desc ? cusort_sort_pairs_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, vb, d_values_in,
+                                                 part_v, n_local, msd_begin, end_bit, stream)
+                  : cusort_sort_pairs(stmp, &stmp_bytes, key_type, d_keys_in, part_k, vb, d_values_in, part_v,
+                                      n_local, msd_begin, end_bit, stream);
+    return desc ? cusort_sort_keys_descending(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin,
+                                              end_bit, stream)
+                : cusort_sort_keys(stmp, &stmp_bytes, key_type, d_keys_in, part_k, n_local, msd_begin, end_bit,
+                                   stream);
+  };
+  bool partitioned = false;
+  if (my_mode != kXchgRouted) {
+    e = partition();
+    if (e) {
+      cudaEventDestroy(counts_ready);
+      return e;
+    }
+    partitioned = true;
   }
 
   // 3. plan (identical on every rank)
@@ -413,76 +485,119 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   cudaEventDestroy(counts_ready);
   if (e) return e;
   std::vector<uint64_t> all_counts((size_t)nranks * 256);
-  bool all_ipc = true;
+  unsigned long long mode = kXchgRouted;
   for (int q = 0; q < nranks; ++q) {
     std::memcpy(&all_counts[(size_t)q * 256], h_all[q].counts, 256 * 8);
-    all_ipc = all_ipc && h_all[q].ipc_ok == 1ull;
+    mode = std::min(mode, h_all[q].mode);
   }
   std::vector<int64_t> send((size_t)nranks), recv((size_t)nranks), totals((size_t)nranks);
-  if (cusort_mgpu_plan(all_counts.data(), nranks, rank, nullptr, send.data(), recv.data(), totals.data()))
+  std::vector<int> owner(256);
+  if (cusort_mgpu_plan(all_counts.data(), nranks, rank, owner.data(), send.data(), recv.data(), totals.data()))
     return cudaErrorInvalidValue;
-  for (int q = 0; q < nranks; ++q)
-    if (totals[q] > out_capacity) return cudaErrorInvalidValue;  // every rank sees it: no rank enters NCCL
+  for (int q = 0; q < nranks; ++q)  // every rank sees the same records: no rank enters NCCL
+    if (totals[q] > (int64_t)h_all[q].cap) return cudaErrorInvalidValue;
   const int64_t n_recv = totals[rank];
 
   // 5. all-to-all
-  if (all_ipc) {
-    // Push this rank's piece for q into q's receive buffers at the offset of
-    // source `rank` (the pieces of lower ranks come first).
-    std::vector<int> owner(256);
-    if (cusort_mgpu_plan(all_counts.data(), nranks, rank, owner.data(), nullptr, nullptr, nullptr))
-      return cudaErrorInvalidValue;
-    int64_t so = 0;
-    for (int q = 0; q < nranks && !e; ++q) {
-      if (send[q] > 0) {
-        int64_t at = 0;  // items q receives from the ranks below this one
-        for (int p = 0; p < rank; ++p)
-          for (int d = 0; d < 256; ++d)
-            if (owner[d] == q) at += (int64_t)all_counts[(size_t)p * 256 + d];
-        uint8_t* dk = nullptr;
-        uint8_t* dv = nullptr;
-        if (q == rank) {
-          dk = rk;
-          dv = rv;
-        } else {
-          e = peer_address(mc, q, h_all[q].hk, h_all[q].off_k, &dk);
-          if (!e && vb) e = peer_address(mc, q, h_all[q].hv, h_all[q].off_v, &dv);
-        }
-        if (!e)
-          e = cudaMemcpyAsync(dk + at * kb, static_cast<uint8_t*>(part_k) + so * kb, (size_t)send[q] * kb,
-                              cudaMemcpyDeviceToDevice, stream);
-        if (!e && vb)
-          e = cudaMemcpyAsync(dv + at * vb, static_cast<uint8_t*>(part_v) + so * vb, (size_t)send[q] * vb,
-                              cudaMemcpyDeviceToDevice, stream);
-      }
-      so += send[q];
+  timer.mark("host");
+  if (mode == kXchgRouted) {
+    // Fused partition + exchange: this rank's items for q go after the items
+    // q receives from lower source ranks, tile by tile.
+    cusort_b200::RouteTable rt;
+    std::memset(&rt, 0, sizeof(rt));
+    for (int d = 255; d >= 0; --d) {
+      rt.owner[d] = (unsigned char)owner[d];
+      rt.first_digit[owner[d]] = (unsigned int)d;
     }
-    // Fence: once every rank's copies (earlier on its stream) are done, the
-    // all-reduce completes everywhere and the received data is complete.
+    for (int d = 0; d < 256; ++d) rt.last_digit[owner[d]] = (unsigned int)d;
+    for (int q = 0; q < nranks; ++q)
+      for (int p = 0; p < rank; ++p)
+        for (int d = 0; d < 256; ++d)
+          if (owner[d] == q) rt.base[q] += all_counts[(size_t)p * 256 + d];
+    bool wide = false;
+    for (int q = 0; q < nranks && !e; ++q) {
+      uint8_t* dk = rk;
+      uint8_t* dv = rv;
+      if (q != rank) {
+        e = peer_address(mc, q, h_all[q].hk, h_all[q].off_k, &dk);
+        if (!e && vb) e = peer_address(mc, q, h_all[q].hv, h_all[q].off_v, &dv);
+      }
+      rt.kptr[q] = reinterpret_cast<unsigned long long>(dk);
+      rt.vptr[q] = vb ? reinterpret_cast<unsigned long long>(dv) : 0ull;
+      rt.cap[q] = h_all[q].cap;
+      wide = wide || (uint64_t)totals[q] > 0xFFFFFFFFull;
+    }
+    if (e) return e;
+    // Pageable source: staged by the driver before the call returns, and the
+    // stream has no pending work here (the records were just waited for).
+    e = cudaMemcpyAsync(t + L.route, &rt, sizeof(rt), cudaMemcpyHostToDevice, stream);
+    if (e) return e;
+    size_t rtb = L.route_tmp_bytes;
+    e = cusort_b200::routed_partition(kt, vb, desc, d_keys_in, d_values_in, n_local, msd_begin, end_bit, wide,
+                                      reinterpret_cast<const cusort_b200::RouteTable*>(t + L.route),
+                                      t + L.route_tmp, &rtb, stream);
+    timer.mark("routed-pass");
+    // Fence: once every rank's routed pass (earlier on its stream) is done,
+    // the all-reduce completes everywhere and the received data is complete.
     if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
     if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
     if (e) return e;
   } else {
-    ncclResult_t r = ncclGroupStart();
-    int64_t so = 0, ro = 0;
-    for (int q = 0; q < nranks && r == ncclSuccess; ++q) {
-      if (send[q] > 0) {
-        r = ncclSend(static_cast<uint8_t*>(part_k) + so * kb, (size_t)send[q] * kb, ncclUint8, q, nc, stream);
-        if (r == ncclSuccess && vb)
-          r = ncclSend(static_cast<uint8_t*>(part_v) + so * vb, (size_t)send[q] * vb, ncclUint8, q, nc, stream);
-      }
-      if (r == ncclSuccess && recv[q] > 0) {
-        r = ncclRecv(rk + ro * kb, (size_t)recv[q] * kb, ncclUint8, q, nc, stream);
-        if (r == ncclSuccess && vb) r = ncclRecv(rv + ro * vb, (size_t)recv[q] * vb, ncclUint8, q, nc, stream);
-      }
-      so += send[q];
-      ro += recv[q];
+    if (!partitioned) {
+      e = partition();
+      if (e) return e;
     }
-    ncclResult_t r2 = ncclGroupEnd();
-    e = nccl_to_cuda(r != ncclSuccess ? r : r2);
-    if (e) return e;
+    if (mode == kXchgCopy) {
+      // Push this rank's piece for q into q's receive buffers at the offset of
+      // source `rank` (the pieces of lower ranks come first).
+      int64_t so = 0;
+      for (int q = 0; q < nranks && !e; ++q) {
+        if (send[q] > 0) {
+          int64_t at = 0;  // items q receives from the ranks below this one
+          for (int p = 0; p < rank; ++p)
+            for (int d = 0; d < 256; ++d)
+              if (owner[d] == q) at += (int64_t)all_counts[(size_t)p * 256 + d];
+          uint8_t* dk = rk;
+          uint8_t* dv = rv;
+          if (q != rank) {
+            e = peer_address(mc, q, h_all[q].hk, h_all[q].off_k, &dk);
+            if (!e && vb) e = peer_address(mc, q, h_all[q].hv, h_all[q].off_v, &dv);
+          }
+          if (!e)
+            e = cudaMemcpyAsync(dk + at * kb, static_cast<uint8_t*>(part_k) + so * kb, (size_t)send[q] * kb,
+                                cudaMemcpyDeviceToDevice, stream);
+          if (!e && vb)
+            e = cudaMemcpyAsync(dv + at * vb, static_cast<uint8_t*>(part_v) + so * vb, (size_t)send[q] * vb,
+                                cudaMemcpyDeviceToDevice, stream);
+        }
+        so += send[q];
+      }
+      if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
+      if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
+      if (e) return e;
+    } else {
+      ncclResult_t r = ncclGroupStart();
+      int64_t so = 0, ro = 0;
+      for (int q = 0; q < nranks && r == ncclSuccess; ++q) {
+        if (send[q] > 0) {
+          r = ncclSend(static_cast<uint8_t*>(part_k) + so * kb, (size_t)send[q] * kb, ncclUint8, q, nc, stream);
+          if (r == ncclSuccess && vb)
+            r = ncclSend(static_cast<uint8_t*>(part_v) + so * vb, (size_t)send[q] * vb, ncclUint8, q, nc, stream);
+        }
+        if (r == ncclSuccess && recv[q] > 0) {
+          r = ncclRecv(rk + ro * kb, (size_t)recv[q] * kb, ncclUint8, q, nc, stream);
+          if (r == ncclSuccess && vb) r = ncclRecv(rv + ro * vb, (size_t)recv[q] * vb, ncclUint8, q, nc, stream);
+        }
+        so += send[q];
+        ro += recv[q];
+      }
+      ncclResult_t r2 = ncclGroupEnd();
+      e = nccl_to_cuda(r != ncclSuccess ? r : r2);
+      if (e) return e;
+    }
   }
 
+  timer.mark("exchange");
   // 6. stable local sort of the received items on every key bit
   if (n_recv >= 2) {
     cusort_double_buffer kd = {{rk, ok_}, 0};
@@ -500,6 +615,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     if (!e && vb) e = cudaMemcpyAsync(d_values_out, rv, vb, cudaMemcpyDeviceToDevice, stream);
     if (e) return e;
   }
+  timer.mark("local-sort");
   if (n_out) *n_out = n_recv;
   return cudaSuccess;
 }

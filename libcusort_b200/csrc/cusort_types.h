@@ -13,6 +13,25 @@ constexpr int kMaxPasses = 8;
 enum : uint32_t {
   kStatusLookbackTimeout = 1u,  // a decoupled-lookback wait ran out of time
   kStatusTmaTimeout = 2u,       // a bulk-copy (TMA) completion wait ran out of time
+  kStatusRouteOverflow = 4u,    // a routed store fell outside its destination buffer (skipped)
+};
+
+// Routing of a partition pass straight into several destination buffers
+// (the multi-GPU exchange).  Digit d belongs to destination q = owner[d]
+// (q < kMaxRouteRanks; each destination owns the contiguous digit range
+// [first_digit[q], last_digit[q]]).  Destination q receives, from item offset
+// base[q] on, every tile's items of its digits: tile by tile, each tile's in
+// the tile's stable digit order.  A tile's run that would reach cap[q] items
+// is skipped and flagged.
+constexpr int kMaxRouteRanks = 64;
+struct RouteTable {
+  unsigned long long base[kMaxRouteRanks];
+  unsigned long long kptr[kMaxRouteRanks];
+  unsigned long long vptr[kMaxRouteRanks];
+  unsigned long long cap[kMaxRouteRanks];
+  unsigned int first_digit[kMaxRouteRanks];
+  unsigned int last_digit[kMaxRouteRanks];
+  unsigned char owner[256];
 };
 
 // Descriptor state, stored in the top two bits of each (tile, digit) word as
@@ -54,7 +73,7 @@ struct OnesweepArgs {
   uint32_t pass;
   uint32_t num_tiles;
   void* desc;              // OffsetT[num_tiles * 256], shared by all passes
-  const void* g_hist_pass; // OffsetT[256] digit counts of this pass
+  const void* g_hist_pass; // OffsetT[256] digit counts of this pass; routed kernels: the RouteTable
   uint32_t* tile_counter;  // dynamic tile ticket of this pass
   uint32_t* status;        // device status word
   uint64_t spin_limit_ns;  // bound on every wait

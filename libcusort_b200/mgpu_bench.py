@@ -21,6 +21,18 @@ def _peaks(root: Path):
     return 6650.0, "fallback 6.65 TB/s"
 
 
+_XCHG_DESC = {
+    "routed": "MSD-digit all-gather, ONE fused partition+exchange onesweep pass storing each item into its "
+              "owner's buffer over NVLink (IPC-mapped peer pointers), NCCL one-word fence, local sort",
+    "copy": "MSD-digit all-gather, partition pass, all-to-all as copy-engine pushes over NVLink into "
+            "IPC-mapped peer buffers, local sort",
+    "nccl": "MSD-digit all-gather, partition pass, all-to-all as grouped ncclSend/ncclRecv, local sort",
+}
+# Library kernels per step: digit count (1) + partition (routed: init + onesweep = 2; otherwise
+# init + histogram + onesweep = 3) + local 4-pass sort (init + histogram + 4 onesweep = 6).
+_LAUNCHES = {"routed": 9, "copy": 10, "nccl": 10}
+
+
 def run(args, torch):
     import torch.distributed as dist
 
@@ -128,6 +140,8 @@ def run(args, torch):
 
         if rank != 0:
             return None
+        mode = os.environ.get("CUSORT_MGPU_EXCHANGE", "routed")
+        mode = mode if mode in _XCHG_DESC else "routed"
         root = Path(__file__).resolve().parents[1]
         peak, peak_src = _peaks(root)
         kb = vb = 4
@@ -141,11 +155,12 @@ def run(args, torch):
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "int32 keys / uint32 values (integer radix)",
             "data": "synthetic (seeded uniform int32 keys per rank, values = global index)",
-            "config": {"workload": "configs[4]-style sharded global sort: MSD-digit all-gather, partition pass, all-to-all (copy-engine pushes over NVLink into IPC-mapped peer buffers), local sort",
+            "config": {"workload": "configs[4]-style sharded global sort: " + _XCHG_DESC[mode],
+                       "exchange": mode,
                        "n_total": n_total, "n_per_gpu": n_local, "parallelism": f"shard{world}",
                        "l2": "inputs per GPU 512 MiB > L2"},
             "verified": {"ranks_sorted": sorted_ok, "ranks_ordered": order_ok, "counts": counts_ok},
-            "gpu_launches": args.steps * 10,
+            "gpu_launches": args.steps * _LAUNCHES[mode],
             "roofline": {"bound": "hbm+nvlink", "achieved_frac_of_pipeline": t_ideal / (ms_step * 1e-3),
                          "t_ideal_ms": t_ideal * 1e3, "local_hbm_bytes_per_gpu": local_bytes,
                          "nvlink_bytes_per_gpu": xchg, "peak_hbm_gbs": peak, "peak_source": peak_src,
