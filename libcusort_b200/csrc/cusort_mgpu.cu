@@ -196,6 +196,17 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
   size_t part_tmp = 0, final_tmp = 0, single_tmp = 0;
   cusort_double_buffer kd = {}, vd = {};
   cudaError_t e;
+  if (nranks == 1) {  // a plain single-GPU sort in the temp storage
+    e = vb ? cusort_sort_pairs(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr, nullptr,
+                               n_local, begin, end, nullptr)
+           : cusort_sort_keys(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, begin, end,
+                              nullptr);
+    if (e) return e;
+    std::memset(L, 0, sizeof(*L));
+    L->sort_tmp_bytes = std::max<size_t>(single_tmp, 1);
+    L->total = a256(L->sort_tmp_bytes);
+    return cudaSuccess;
+  }
   if (vb) {
     e = desc ? cusort_sort_pairs_descending(nullptr, &part_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr,
                                             nullptr, n_local, msd_begin, end, nullptr)
@@ -205,15 +216,10 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
     e = desc ? cusort_sort_pairs_descending_db(nullptr, &final_tmp, (cusort_key_type)kt, &kd, vb, &vd, cap, begin,
                                                end, nullptr)
              : cusort_sort_pairs_db(nullptr, &final_tmp, (cusort_key_type)kt, &kd, vb, &vd, cap, begin, end, nullptr);
-    if (e) return e;
-    e = cusort_sort_pairs(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr, nullptr,
-                          n_local, begin, end, nullptr);
   } else {
     e = cusort_sort_keys(nullptr, &part_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, msd_begin, end, nullptr);
     if (e) return e;
     e = cusort_sort_keys_db(nullptr, &final_tmp, (cusort_key_type)kt, &kd, cap, begin, end, nullptr);
-    if (e) return e;
-    e = cusort_sort_keys(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, begin, end, nullptr);
   }
   if (e) return e;
   size_t route_tmp = 0;
@@ -239,7 +245,7 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
   L->alt_v = o;
   o += a256((size_t)cap * vb);
   L->sort_tmp = o;
-  L->sort_tmp_bytes = std::max(std::max(part_tmp, final_tmp), std::max<size_t>(single_tmp, 1));
+  L->sort_tmp_bytes = std::max(std::max(part_tmp, final_tmp), size_t(1));
   o += a256(L->sort_tmp_bytes);
   L->total = o;
   return cudaSuccess;

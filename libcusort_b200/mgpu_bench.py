@@ -1,8 +1,12 @@
 """bench.py's N>1 path: the sharded multi-GPU sort, one rank per GPU.
 
-Weak scaling: every rank sorts 2^log2n int32 keys + uint32 values (its slice
-of the global input, values = global index); value = all ranks' items / the
-slowest rank's time.  --total-log2n instead fixes the global size (strong).
+Default: strong scaling of the global 2^32-item sort of uint32
+keys (uniform, seeded per rank) with uint32 values = global index, split
+evenly over the ranks (--total-log2n changes the global size).  --weak
+instead gives every rank 2^log2n items.  value = all ranks' items / the
+slowest rank's time.  The end-to-end figure (pinned host slice -> device ->
+sharded sort -> host) runs the same call on a bounded sample of at most
+2^28 items per GPU, stated in the JSON line.
 """
 from __future__ import annotations
 
@@ -61,20 +65,28 @@ def run(args, torch):
     sorter = None
     try:
         sorter = mgpu.ShardedSorter.from_torch_distributed()
-        if getattr(args, "total_log2n", None):
-            n_total = 1 << args.total_log2n
-            scaling = "strong"
-        else:
+        if getattr(args, "weak", False):
             n_total = (1 << args.log2n) * world
             scaling = "weak"
+        else:
+            n_total = 1 << (args.total_log2n or 32)
+            scaling = "strong"
         n_local = n_total // world + (1 if rank < n_total % world else 0)
         first = rank * (n_total // world) + min(rank, n_total % world)
         g = torch.Generator(device=dev)
         g.manual_seed(1000 + rank)
-        keys = torch.randint(-(2 ** 31), 2 ** 31, (n_local,), dtype=torch.int64, device=dev, generator=g).to(torch.int32)
-        vals = torch.arange(first, first + n_local, dtype=torch.int64, device=dev).to(torch.int32)
+        # uint32 keys (the int32 bit pattern, sorted as unsigned) and uint32 global-index values
+        keys = torch.empty(n_local, dtype=torch.int32, device=dev)
+        vals = torch.empty(n_local, dtype=torch.int32, device=dev)
+        chunk = 1 << 27
+        for s0 in range(0, n_local, chunk):
+            m = min(chunk, n_local - s0)
+            keys[s0:s0 + m] = torch.randint(-(2 ** 31), 2 ** 31, (m,), dtype=torch.int64, device=dev,
+                                            generator=g).to(torch.int32)
+            vals[s0:s0 + m] = torch.arange(first + s0, first + s0 + m, dtype=torch.int64, device=dev).to(torch.int32)
+        keys = keys.view(torch.uint32) if hasattr(torch, "uint32") else keys
         cap = int(n_local * 1.5) + 65536
-        out_k = torch.empty(cap, dtype=torch.int32, device=dev)
+        out_k = torch.empty(cap, dtype=keys.dtype, device=dev)
         out_v = torch.empty(cap, dtype=torch.int32, device=dev)
 
         def step():
@@ -97,11 +109,14 @@ def run(args, torch):
         dist.barrier()
         ms_step = ms.item() / args.steps
 
-        # verification: each rank sorted, ranks ordered, counts add up
+        # verification: each rank sorted, ranks ordered, counts add up (unsigned
+        # order checked as signed order of the bit pattern with the top bit flipped)
         n_mine = ko.numel()
-        ok_local = bool((ko[1:] >= ko[:-1]).all().item()) if n_mine > 1 else True
-        lo = ko[0].item() if n_mine else 2 ** 31 - 1
-        hi = ko[-1].item() if n_mine else -(2 ** 31)
+        ks = ko.view(torch.int32) ^ (-(2 ** 31))
+        ok_local = bool((ks[1:] >= ks[:-1]).all().item()) if n_mine > 1 else True
+        lo = ks[0].item() if n_mine else 2 ** 31 - 1
+        hi = ks[-1].item() if n_mine else -(2 ** 31)
+        del ks
         stats = [None] * world
         dist.all_gather_object(stats, (n_mine, lo, hi, ok_local, int(n_local)))
         counts_ok = sum(s[0] for s in stats) == n_total
@@ -109,17 +124,22 @@ def run(args, torch):
                        if stats[i][0] and stats[j][0])
         sorted_ok = all(s[3] for s in stats)
 
-        # e2e: pinned host slice -> H2D -> sharded sort -> D2H of this rank's part
-        kh = keys.cpu().pin_memory()
-        vh = vals.cpu().pin_memory()
-        okh = torch.empty(cap, dtype=torch.int32, pin_memory=True)
-        ovh = torch.empty(cap, dtype=torch.int32, pin_memory=True)
-        kd, vd = torch.empty_like(keys), torch.empty_like(vals)
+        # e2e: pinned host slice -> H2D -> sharded sort -> D2H of this rank's part,
+        # on a sample of at most 2^28 items per GPU (the first items of each slice)
+        e_local = min(n_local, 1 << 28)
+        e_total = sum(min(n_total // world + (1 if r < n_total % world else 0), 1 << 28) for r in range(world))
+        e_cap = int(e_local * 1.5) + 65536
+        kh = keys[:e_local].cpu().pin_memory()
+        vh = vals[:e_local].cpu().pin_memory()
+        okh = torch.empty(e_cap, dtype=keys.dtype, pin_memory=True)
+        ovh = torch.empty(e_cap, dtype=torch.int32, pin_memory=True)
+        kd, vd = keys[:e_local].clone(), vals[:e_local].clone()
+        del keys, vals
 
         def e2e_step():
             kd.copy_(kh, non_blocking=True)
             vd.copy_(vh, non_blocking=True)
-            k2, v2 = sorter.sort(kd, vd, capacity=cap, out_keys=out_k, out_values=out_v)
+            k2, v2 = sorter.sort(kd, vd, capacity=e_cap, out_keys=out_k[:e_cap], out_values=out_v[:e_cap])
             m = k2.numel()
             okh[:m].copy_(k2, non_blocking=True)
             ovh[:m].copy_(v2, non_blocking=True)
@@ -150,23 +170,24 @@ def run(args, torch):
         xchg = n_local * (kb + vb) * (world - 1) / world  # expected bytes each GPU sends over NVLink
         t_ideal = local_bytes / (peak * 1e9) + xchg / 770e9
         return {
-            "metric": "Gkeys/s (sharded int32/uint32 SortPairs across GPUs)", "value": n_total / (ms_step * 1e-3) / 1e9,
+            "metric": "Gkeys/s (sharded uint32/uint32 SortPairs across GPUs)", "value": n_total / (ms_step * 1e-3) / 1e9,
             "unit": "Gkeys/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
-            "dtype": "int32 keys / uint32 values (integer radix)",
-            "data": "synthetic (seeded uniform int32 keys per rank, values = global index)",
+            "dtype": "uint32 keys / uint32 values (integer radix)",
+            "data": "synthetic (seeded uniform uint32 keys per rank, values = global index)",
             "config": {"workload": "configs[4]-style sharded global sort: " + _XCHG_DESC[mode],
                        "exchange": mode,
                        "n_total": n_total, "n_per_gpu": n_local, "parallelism": f"shard{world}",
-                       "l2": "inputs per GPU 512 MiB > L2"},
+                       "l2": f"inputs per GPU {n_local * 8 / 2**20:.0f} MiB > L2"},
             "verified": {"ranks_sorted": sorted_ok, "ranks_ordered": order_ok, "counts": counts_ok},
             "gpu_launches": args.steps * _LAUNCHES[mode],
             "roofline": {"bound": "hbm+nvlink", "achieved_frac_of_pipeline": t_ideal / (ms_step * 1e-3),
                          "t_ideal_ms": t_ideal * 1e3, "local_hbm_bytes_per_gpu": local_bytes,
                          "nvlink_bytes_per_gpu": xchg, "peak_hbm_gbs": peak, "peak_source": peak_src,
                          "nvlink_gbs": 770.0, "nvlink_source": "measured peer copy per direction on this pool"},
-            "e2e": {"value": n_total / (e_ms * 1e-3) / 1e9, "unit": "Gkeys/s", "ms_per_step": e_ms,
-                    "h2d_bytes_per_step": n_total * (kb + vb), "d2h_bytes_per_step": n_total * (kb + vb)},
+            "e2e": {"value": e_total / (e_ms * 1e-3) / 1e9, "unit": "Gkeys/s", "ms_per_step": e_ms,
+                    "sample": f"{e_total} items ({e_total // world} per GPU) of the same workload",
+                    "h2d_bytes_per_step": e_total * (kb + vb), "d2h_bytes_per_step": e_total * (kb + vb)},
         }
     finally:
         if sorter is not None:
