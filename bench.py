@@ -54,7 +54,9 @@ def parse():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--total-log2n", type=int, default=None,
-                    help="N>1: fix the global item count at 2^this (strong scaling) instead of 2^log2n per GPU")
+                    help="N>1: global item count 2^this, split over the GPUs (strong scaling; default 32, configs[4])")
+    ap.add_argument("--weak", action="store_true",
+                    help="N>1: 2^log2n items per GPU (weak scaling) instead of the fixed global size")
     ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs"], default=None,
                     help="only run --warmup + --steps sorts of this case (for ncu captures)")
     return ap.parse_args()
