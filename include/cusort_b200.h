@@ -156,6 +156,33 @@ cudaError_t cusort_sort_db_noalloc(cusort_key_type key_type, cusort_double_buffe
                                    cusort_double_buffer* d_values, int64_t num_items, int begin_bit, int end_bit,
                                    int descending, cudaStream_t stream);
 
+/* ---- segmented sort ----------------------------------------------------
+ * The reference names segmented sorting in its banner (libcusort.cuh:4) but
+ * implements none; the interface follows CUB's DeviceSegmentedRadixSort.
+ * Every segment [d_begin_offsets[s], d_end_offsets[s]) of the input is sorted
+ * independently and stably (same key order, bit range and direction rules as
+ * cusort_sort_keys / cusort_sort_pairs) into the same positions of the
+ * output.  Positions outside every segment are not written; end <= begin is
+ * an empty segment; segments must not overlap (overlap that exceeds the
+ * planned work sets status bit 3, value 8, and leaves the long segments
+ * unsorted).  Offsets are int64 arrays in device memory.  Two-phase temp
+ * protocol; the size depends only on num_items, the key/value types and the
+ * bit range, not on the offsets, and no call synchronises the stream.
+ * Segments of up to a few thousand items are sorted in one warp or one CTA
+ * (every pass in shared memory); longer ones by onesweep passes whose tiles
+ * never straddle a segment. */
+cudaError_t cusort_segmented_sort_keys(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                                       const void* d_keys_in, void* d_keys_out, int64_t num_items,
+                                       int64_t num_segments, const int64_t* d_begin_offsets,
+                                       const int64_t* d_end_offsets, int begin_bit, int end_bit, int descending,
+                                       cudaStream_t stream);
+cudaError_t cusort_segmented_sort_pairs(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                                        const void* d_keys_in, void* d_keys_out, size_t value_bytes,
+                                        const void* d_values_in, void* d_values_out, int64_t num_items,
+                                        int64_t num_segments, const int64_t* d_begin_offsets,
+                                        const int64_t* d_end_offsets, int begin_bit, int end_bit, int descending,
+                                        cudaStream_t stream);
+
 /* ---- sharded multi-GPU sort over NCCL (no counterpart in the reference,
  *      which is single-GPU only) ------------------------------------------
  * One process (or thread) per GPU.  Rank r passes its contiguous slice of
@@ -211,7 +238,9 @@ int cusort_set_launch_mode(int mode);
 /* Device status word of the last sort that used this temp storage:
  * 0 = ok, bit 0 = a lookback wait timed out, bit 1 = a tile-copy wait timed
  * out, bit 2 = (cusort_mgpu_sort temp storage) a partition store fell outside
- * its destination buffer and was skipped.  Synchronises `stream`. */
+ * its destination buffer and was skipped, bit 3 = (segmented sort temp
+ * storage) the segments needed more work than planned (overlapping segments).
+ * Synchronises `stream`. */
 cudaError_t cusort_read_device_status(const void* d_temp_storage, uint32_t* status, cudaStream_t stream);
 
 /* Bound on every device-side wait, in nanoseconds (default 2e9).  Per host

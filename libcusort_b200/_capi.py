@@ -42,6 +42,9 @@ SIGNATURES = {
     "cusort_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_wide": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _i, _vp]),
+    "cusort_segmented_sort_keys": (_i, [_vp, _P_SZ, _i, _vp, _vp, _i64, _i64, _vp, _vp, _i, _i, _i, _vp]),
+    "cusort_segmented_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i64, _vp, _vp, _i, _i, _i,
+                                         _vp]),
     "cusort_sort_db_noalloc": (_i, [_i, _P_DB, _sz, _P_DB, _i64, _i, _i, _i, _vp]),
     "cusort_mgpu_unique_id": (_i, [C.c_char_p]),
     "cusort_mgpu_comm_init": (_i, [C.POINTER(C.c_void_p), C.c_char_p, _i, _i]),

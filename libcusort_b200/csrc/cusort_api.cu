@@ -642,6 +642,19 @@ cudaError_t routed_partition(int kt, size_t vb, bool desc, const void* keys, con
   return launch_direct(ls, stream);
 }
 
+void twiddle_constants_of(int kt, bool desc, uint64_t* c, uint64_t* f) {
+  twiddle_constants(kt, key_bytes_of(kt), desc, c, f);
+}
+
+uint64_t wait_limit_ns() { return g_ts.wait_limit_ns; }
+
+cudaError_t occupancy_of(const KernelInfo& k, int* sms, int* ctas_per_sm) {
+  int dev = 0;
+  CUSORT_TRY(cudaGetDevice(&dev));
+  CUSORT_TRY(get_sm_count(dev, sms));
+  return get_occupancy(dev, k, ctas_per_sm);
+}
+
 // DoubleBuffer sort whose temp storage is a caller-provided scratch region
 // of `scratch_bytes` (used by the no-allocation entry point): rejects calls
 // whose temp storage would not fit, and always launches directly.

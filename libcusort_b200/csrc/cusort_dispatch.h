@@ -27,6 +27,15 @@ bool get_kernels_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* 
 bool get_routed_k12(int key_bytes, int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
 bool get_routed_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
 bool get_routed_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
+// Segmented-sort kernels (kernels_seg_*.cu; cusort_segmented.cuh).
+struct SegKernels {
+  KernelInfo onesweep, hist, scan, small_warp, small_block;
+};
+bool get_segmented_k12(int key_bytes, int value_bytes, int off_bytes, bool float_key, SegKernels* k);
+bool get_segmented_k4(int value_bytes, int off_bytes, bool float_key, SegKernels* k);
+bool get_segmented_k8(int value_bytes, int off_bytes, bool float_key, SegKernels* k);
+const void* get_seg_plan_kernel();
+const void* get_seg_copy_kernel(int bytes);
 const void* get_init_kernel();
 // Count-and-fill kernel of 1-byte keys-only full-range sorts (kernels_k1.cu).
 const void* get_fill_bytes_kernel(int off_bytes);
@@ -39,6 +48,13 @@ cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type
 // Single-digit counts (u64[256]) of the twiddled keys (cusort_api.cu).
 cudaError_t digit_counts_u64(int key_type, bool descending, const void* keys, int64_t num_items, int begin_bit,
                              int end_bit, unsigned long long* d_counts, cudaStream_t stream);
+
+// Twiddle constants of a key type (cusort_api.cu) and the calling thread's
+// bound on device-side waits (cusort_set_wait_limit_ns).
+void twiddle_constants_of(int key_type, bool descending, uint64_t* c, uint64_t* f);
+uint64_t wait_limit_ns();
+// Resident CTAs per SM of a kernel on the current device (cached).
+cudaError_t occupancy_of(const KernelInfo& k, int* sms, int* ctas_per_sm);
 
 struct RouteTable;
 // One stable partition pass over the digit [begin_bit, end_bit) (at most 8

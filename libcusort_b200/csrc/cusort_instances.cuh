@@ -11,6 +11,7 @@
 
 #include "cusort_dispatch.h"
 #include "cusort_kernels.cuh"
+#include "cusort_segmented.cuh"
 
 namespace cusort_b200 {
 
@@ -52,10 +53,10 @@ struct TileShape {
 constexpr int kHistThreads = 1024;
 constexpr int kHistUnroll = 4;
 
-template <int KB, int VB, typename Off, bool FK, bool ROUTED = false>
+template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG = false>
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB>;
-  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED>;
+  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>;
   os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;
   os->tile = CFG::TILE;
@@ -121,6 +122,55 @@ inline bool get_routed_impl(int vb, int offb, bool float_key, KernelInfo* os) {
   }
   if (offb == 4) return fill_for_value<KB, unsigned int, false, true>(vb, os);
   if (offb == 8) return fill_for_value<KB, unsigned long long, false, true>(vb, os);
+  return false;
+}
+
+// Segmented sort kernels for one (key width, value width, offset width, float).
+template <int KB, int VB, typename Off, bool FK>
+inline void fill_segmented(SegKernels* k) {
+  fill_onesweep<KB, VB, Off, FK, false, true>(&k->onesweep);
+  k->hist.func = reinterpret_cast<const void*>(&seg_hist_kernel<KB, Off, FK>);
+  k->hist.threads = 512;
+  k->hist.smem = (size_t)KB * kRadix * 4;  // at most KB passes
+  k->scan.func = reinterpret_cast<const void*>(&seg_scan_kernel<Off>);
+  k->scan.threads = 256;
+  constexpr int KPT = SegSmallShape<KB, VB>::KPT;
+  k->small_warp.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 1, KPT>);
+  k->small_warp.threads = 256;
+  k->small_warp.tile = SegSmallLayout<KB, VB, FK, 1, KPT>::CAP;
+  k->small_warp.smem = SegSmallLayout<KB, VB, FK, 1, KPT>::SMEM;
+  k->small_block.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 8, KPT>);
+  k->small_block.threads = 256;
+  k->small_block.tile = SegSmallLayout<KB, VB, FK, 8, KPT>::CAP;
+  k->small_block.smem = SegSmallLayout<KB, VB, FK, 8, KPT>::SMEM;
+}
+
+template <int KB, typename Off, bool FK>
+inline bool fill_segmented_vb(int vb, SegKernels* k) {
+  switch (vb) {
+    case 0: fill_segmented<KB, 0, Off, FK>(k); return true;
+    case 1: fill_segmented<KB, 1, Off, FK>(k); return true;
+    case 2: fill_segmented<KB, 2, Off, FK>(k); return true;
+    case 4: fill_segmented<KB, 4, Off, FK>(k); return true;
+    case 8: fill_segmented<KB, 8, Off, FK>(k); return true;
+    case 16: fill_segmented<KB, 16, Off, FK>(k); return true;
+    default: return false;
+  }
+}
+
+template <int KB>
+inline bool get_segmented_impl(int vb, int offb, bool float_key, SegKernels* k) {
+  if constexpr (KB == 4 || KB == 8) {
+    if (float_key) {
+      if (offb == 4) return fill_segmented_vb<KB, unsigned int, true>(vb, k);
+      if (offb == 8) return fill_segmented_vb<KB, unsigned long long, true>(vb, k);
+      return false;
+    }
+  } else {
+    if (float_key) return false;
+  }
+  if (offb == 4) return fill_segmented_vb<KB, unsigned int, false>(vb, k);
+  if (offb == 8) return fill_segmented_vb<KB, unsigned long long, false>(vb, k);
   return false;
 }
 

@@ -451,13 +451,18 @@ struct RankSlots {
 #define CUSORT_RANK_MODE_OF(KB, VB) \
   (CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE : (((VB) == 0 && (KB) <= 4) ? CUSORT_KEYS_RANK_MODE : 4))
 
-template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_, bool ROUTED_ = false>
+template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_, bool ROUTED_ = false,
+          bool SEG_ = false>
 struct OnesweepCfg {
   static constexpr int KB = KB_, VB = VB_, THREADS = THREADS_, KPT = KPT_, MINB = MINB_;
   static constexpr bool FLOAT_KEY = FLOAT_KEY_;
   // Routed pass (multi-GPU partition): digit bases and destinations come from
   // a RouteTable, stores may target peers' memory.
   static constexpr bool ROUTED = ROUTED_;
+  // Segmented pass: tiles of multi-tile segments (SegOnesweepArgs).
+  static constexpr bool SEG = SEG_;
+  static_assert(!(ROUTED && SEG), "one special mode at a time");
+  using Args = typename std::conditional<SEG, SegOnesweepArgs, OnesweepArgs>::type;
   // Measured on B200 (2^26 items): mode 4 is fastest for pairs and 8-byte
   // keys; for keys-only <= 4 bytes its extra registers spill and mode 3 wins.
   static constexpr int RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
@@ -531,20 +536,21 @@ struct DescBits {
 // digit's thread reads a window of W predecessor words per round trip
 // (independent loads), adds aggregates from the nearest outward and stops at
 // the first INCLUSIVE word; an EMPTY word ends the window and is re-polled
-// (bounded wait).  Tile 0 has no predecessors.
+// (bounded wait).  Tile `floor` (0, or a segment's first tile) has no
+// predecessors.
 template <typename Off, int W>
 __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, uint32_t digit, uint32_t pass,
-                                               uint32_t* status, uint64_t limit_ns) {
+                                               uint32_t* status, uint64_t limit_ns, int64_t floor = 0) {
   using DB = DescBits<Off>;
   Off excl = 0;
   int64_t j = (int64_t)tile - 1;  // nearest predecessor not yet accounted for
   dev::SpinGuard guard;
-  while (j >= 0) {
+  while (j >= floor) {  // floor: first tile of the prefix (a segment's first tile)
     Off w[W];
 #pragma unroll
     for (int k = 0; k < W; ++k)
-      w[k] = (j - k >= 0) ? dev::ld_relaxed(desc + (size_t)(j - k) * kRadix + digit)
-                          : DB::make(pass, kDescInclusive, Off(0));
+      w[k] = (j - k >= floor) ? dev::ld_relaxed(desc + (size_t)(j - k) * kRadix + digit)
+                              : DB::make(pass, kDescInclusive, Off(0));
     int consumed = 0;
     bool done = false;
 #pragma unroll
@@ -567,7 +573,7 @@ __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, u
 }
 
 template <class CFG>
-__global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const OnesweepArgs a) {
+__global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const typename CFG::Args a) {
   using K = typename dev::UIntOf<CFG::KB>::T;
   using V = typename dev::UIntOf<(CFG::VB ? CFG::VB : 1)>::T;
   using Off = typename CFG::Off;
@@ -593,12 +599,13 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   const V* vals_in = static_cast<const V*>(a.vals_in);
   V* vals_out = static_cast<V*>(a.vals_out);
   Off* desc = static_cast<Off*>(a.desc);
-  const uint32_t num_tiles = a.num_tiles;
+  uint32_t num_tiles = a.num_tiles;  // segmented: the planner's count, read after the PDL wait
   const bool tma_ok = a.tma_keys && (!HAS_V || a.tma_vals);
   const uint64_t pol = dev::l2_policy_evict_first();
 
   // A tile is staged by TMA when it is full and both inputs are 16-byte aligned.
   auto tma_tile = [&](uint32_t t) {
+    if constexpr (CFG::SEG) return false;  // segment tiles start anywhere: cooperative loads
     return !CFG::DIRECT_LOAD && tma_ok && t < num_tiles && (uint64_t)(t + 1) * TILE <= a.n;
   };
   auto issue_tma = [&](uint32_t t, int buf) {
@@ -628,7 +635,12 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 
   // Global exclusive offset of every digit for this pass (from the upfront
   // histogram), computed once per CTA; the first tile ticket is taken here.
-  if constexpr (CFG::ROUTED) {
+  if constexpr (CFG::SEG) {
+    // per-segment digit bases are loaded per tile
+    num_tiles = a.ctl->num_tiles;
+    if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
+    __syncthreads();
+  } else if constexpr (CFG::ROUTED) {
     // Destinations: owner of each digit; per owner its buffers, capacity,
     // this rank's offset in it and its first digit.
     unsigned char* s_owner = smem + CFG::OFF_ROUTE;
@@ -705,8 +717,23 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       }
     }
     const uint32_t tile = cur;
-    const uint64_t base = (uint64_t)tile * TILE;
-    const uint32_t valid = (uint32_t)((a.n - base) < (uint64_t)TILE ? (a.n - base) : (uint64_t)TILE);
+    uint64_t base;
+    uint32_t valid;
+    uint32_t floor = 0;  // first tile of this tile's prefix chain
+    if constexpr (CFG::SEG) {
+      // the tile's segment, its place in it, and the segment's digit bases
+      const uint32_t slot = a.tile_slot[tile];
+      const SegRecord r = a.recs[slot];
+      const uint64_t i = (uint64_t)(tile - r.tile_first) * TILE;
+      base = r.begin + i;
+      valid = (uint32_t)((r.len - i) < (uint64_t)TILE ? (r.len - i) : (uint64_t)TILE);
+      floor = r.tile_first;
+      if (tid < kRadix)
+        s_gbase[tid] = static_cast<const Off*>(a.seg_gbase)[((size_t)slot * a.seg_passes + a.seg_pass) * kRadix + tid];
+    } else {
+      base = (uint64_t)tile * TILE;
+      valid = (uint32_t)((a.n - base) < (uint64_t)TILE ? (a.n - base) : (uint64_t)TILE);
+    }
     const bool publish = (int64_t)tile != a.skip_tile;
     K* s_keys = reinterpret_cast<K*>(smem + (size_t)b * CFG::BUF_BYTES);
     V* s_vals = reinterpret_cast<V*>(smem + (size_t)b * CFG::BUF_BYTES + CFG::KEYS_BYTES);
@@ -802,7 +829,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       if (tid == a.mask) cnt -= (uint32_t)TILE - valid;
       if (publish)
         dev::st_relaxed(desc + (size_t)tile * kRadix + tid,
-                        DB::make(a.pass, tile == 0 ? kDescInclusive : kDescAggregate, (Off)cnt));
+                        DB::make(a.pass, tile == floor ? kDescInclusive : kDescAggregate, (Off)cnt));
     }
     uint32_t incl = 0;
     if (warp < kRadix / 32) {
@@ -854,8 +881,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     // warps' reorder work instead of trailing it.
     if (tid < kRadix) {
       Off excl = 0;
-      if (tile > 0) {
-        excl = lookback_prefix<Off, kLookbackWindow>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns);
+      if (tile > floor) {
+        excl = lookback_prefix<Off, kLookbackWindow>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, floor);
         if (publish)
           dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
       }

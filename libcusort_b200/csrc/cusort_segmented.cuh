@@ -1,0 +1,258 @@
+// cusort_segmented.cuh -- kernels of the segmented sort (each segment
+// [begin[s], end[s]) of the input sorted independently, stable, into the same
+// positions of the output).  The reference names segmented sorting in its
+// banner (libcusort.cuh:4) but implements none; the interface follows CUB's
+// DeviceSegmentedRadixSort (begin/end offset arrays in device memory).
+//
+// Segments are handled by length class, with no host synchronisation:
+//   * up to 32*KPT items: one warp per segment, every pass in shared memory
+//     (seg_small_kernel<..., WPS = 1>);
+//   * up to 256*KPT items: one 256-thread CTA per segment, same scheme
+//     (seg_small_kernel<..., WPS = 8>);
+//   * longer: cut into onesweep tiles that never straddle a segment.  The
+//     planner (seg_plan_kernel) gives each such segment a slot and a run of
+//     tile numbers, seg_hist_kernel counts every pass's digits per segment,
+//     seg_scan_kernel turns the counts into segment-local digit bases, and
+//     each pass is onesweep_kernel with SEG = true (lookback stops at the
+//     segment's first tile).
+#pragma once
+
+#include "cusort_device.cuh"
+#include "cusort_types.h"
+
+namespace cusort_b200 {
+
+enum : uint32_t { kStatusSegOverflow = 8u };  // more tiles/segments than planned (overlapping segments)
+
+// Items per thread of the small-segment sorts, by bytes per item.
+template <int KB, int VB>
+struct SegSmallShape {
+  static constexpr int BYTES = KB + VB;
+  static constexpr int KPT = BYTES <= 8 ? 16 : (BYTES <= 16 ? 8 : 4);
+};
+
+// ---------------------------------------------------------------------------
+// small segments: WPS warps sort one segment of at most WPS*32*KPT items, all
+// passes in shared memory, then one coalesced write.  Per pass: each warp
+// ranks its slots in order with __match_any_sync (rank among equal digits =
+// earlier slots' count + lower lanes of this slot), the group turns the
+// per-warp digit counts into offsets (digit-major, warp-minor: stable), and
+// every item is stored at its offset (in place: all items are in registers).
+// ---------------------------------------------------------------------------
+template <int KB, int VB, bool FK, int WPS, int KPT>
+struct SegSmallLayout {
+  static constexpr int CAP = WPS * 32 * KPT;
+  static constexpr size_t KEYS = ((size_t)CAP * KB + 15) / 16 * 16;
+  static constexpr size_t VALS = ((size_t)CAP * (VB ? VB : 1) + 15) / 16 * 16;
+  static constexpr size_t CNT = (size_t)WPS * kRadix * 4;
+  static constexpr size_t SCAN = 16 * 4;
+  static constexpr size_t GROUP = KEYS + VALS + CNT + SCAN;
+  static constexpr int GROUPS = 8 / WPS;
+  static constexpr size_t SMEM = GROUP * GROUPS;
+};
+
+template <int KB, int VB, bool FK, int WPS, int KPT>
+__global__ void __launch_bounds__(256) seg_small_kernel(const SegSmallArgs a) {
+  using K = typename dev::UIntOf<KB>::T;
+  using V = typename dev::UIntOf<(VB ? VB : 1)>::T;
+  using L = SegSmallLayout<KB, VB, FK, WPS, KPT>;
+  constexpr bool HAS_V = VB > 0;
+  constexpr int GT = WPS * 32;  // threads per group
+  extern __shared__ __align__(16) uint8_t smem[];
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t g = warp / WPS, wg = warp % WPS, gtid = tid % GT;
+  uint8_t* gb = smem + (size_t)g * L::GROUP;
+  K* sk = reinterpret_cast<K*>(gb);
+  V* sv = reinterpret_cast<V*>(gb + L::KEYS);
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS);  // [WPS][256]
+  uint32_t* scan = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS + L::CNT);
+  auto gsync = [&]() {
+    if constexpr (WPS == 1) __syncwarp();
+    else __syncthreads();
+  };
+  const K* keys_in = static_cast<const K*>(a.keys_in);
+  K* keys_out = static_cast<K*>(a.keys_out);
+  const V* vals_in = static_cast<const V*>(a.vals_in);
+  V* vals_out = static_cast<V*>(a.vals_out);
+  const K tc = (K)a.tw_c, tf = (K)a.tw_f;
+  const uint32_t lt = dev::lanemask_lt();
+
+  const uint64_t groups = (uint64_t)gridDim.x * L::GROUPS;
+  for (uint64_t s = (uint64_t)blockIdx.x * L::GROUPS + g; s < a.num_segments; s += groups) {
+    const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
+    const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
+    if (len < a.min_len || len > a.max_len || len == 0) continue;  // uniform within the group
+    const uint32_t n = (uint32_t)len;
+    for (uint32_t i = gtid; i < n; i += GT) {
+      sk[i] = keys_in[b + i];
+      if constexpr (HAS_V) sv[i] = vals_in[b + i];
+    }
+    gsync();
+    for (uint32_t p = 0; p < a.passes; ++p) {
+      const uint32_t shift = a.begin_bit + 8u * p;
+      const uint32_t mask = (p + 1 == a.passes) ? a.last_mask : 0xffu;
+      uint32_t* wc = cnt + wg * kRadix;
+      for (uint32_t d = lane; d < kRadix; d += 32) wc[d] = 0;
+      __syncwarp();
+      K key[KPT];
+      V val[HAS_V ? KPT : 1];
+      uint32_t rd[KPT];  // digit (9 bits, 0x100 = past the end) | rank within the warp << 9
+      const uint32_t wfirst = wg * KPT * 32;
+#pragma unroll
+      for (int sl = 0; sl < KPT; ++sl) {
+        const uint32_t i = wfirst + sl * 32 + lane;
+        const bool in = i < n;
+        key[sl] = in ? sk[i] : K(0);
+        if constexpr (HAS_V) val[sl] = in ? sv[i] : V{};
+        const uint32_t d = in ? dev::digit_k<FK, K>(key[sl], tc, tf, shift, mask) : 0x100u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        uint32_t before = 0;
+        if (in) before = wc[d];
+        __syncwarp();
+        if (in && (peers & lt) == 0) wc[d] = before + __popc(peers);
+        __syncwarp();
+        rd[sl] = d | ((before + __popc(peers & lt)) << 9);
+      }
+      gsync();
+      // digit totals -> offsets[w][d] = start of digit d + items of d in lower warps
+      if constexpr (WPS == 8) {
+        const uint32_t d = tid;  // 256 threads, one digit each
+        uint32_t tot = 0;
+#pragma unroll
+        for (int w = 0; w < WPS; ++w) tot += cnt[w * kRadix + d];
+        const uint32_t incl = dev::warp_inclusive_scan(tot, lane);
+        if (lane == 31) scan[warp] = incl;
+        __syncthreads();
+        uint32_t start = incl - tot;
+        for (uint32_t w = 0; w < warp; ++w) start += scan[w];
+#pragma unroll
+        for (int w = 0; w < WPS; ++w) {
+          const uint32_t c = cnt[w * kRadix + d];
+          cnt[w * kRadix + d] = start;
+          start += c;
+        }
+      } else {
+        // one warp: lane handles digits 8*lane .. 8*lane+7
+        uint32_t c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = cnt[lane * 8 + j];
+          sum += c[j];
+        }
+        uint32_t start = dev::warp_inclusive_scan(sum, lane) - sum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          cnt[lane * 8 + j] = start;
+          start += c[j];
+        }
+      }
+      gsync();
+#pragma unroll
+      for (int sl = 0; sl < KPT; ++sl) {
+        const uint32_t d = rd[sl] & 0x1ffu;
+        if (d < kRadix) {
+          const uint32_t pos = cnt[wg * kRadix + d] + (rd[sl] >> 9);
+          sk[pos] = key[sl];
+          if constexpr (HAS_V) sv[pos] = val[sl];
+        }
+      }
+      gsync();
+    }
+    for (uint32_t i = gtid; i < n; i += GT) {
+      keys_out[b + i] = sk[i];
+      if constexpr (HAS_V) vals_out[b + i] = sv[i];
+    }
+    gsync();  // the buffers are reused by the next segment
+  }
+}
+
+// ---------------------------------------------------------------------------
+// planner: a slot and a run of tile numbers for every segment longer than
+// min_len (atomic allocation: each segment's tiles are consecutive, which is
+// all the lookback needs).  Capacity is checked; an overflow (only possible
+// with overlapping segments) sets kStatusSegOverflow and ctl->pad[0], and the
+// tiled kernels then do nothing.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) seg_plan_kernel(const SegPlanArgs a);
+
+// ---------------------------------------------------------------------------
+// per-segment digit counts of every pass, one tile at a time
+// ---------------------------------------------------------------------------
+template <int KB, typename Off, bool FK>
+__global__ void __launch_bounds__(512) seg_hist_kernel(const SegHistArgs a) {
+  using K = typename dev::UIntOf<KB>::T;
+  extern __shared__ __align__(16) uint32_t s_cnt[];  // [passes][256]
+  dev::pdl_wait();
+  dev::pdl_launch_dependents();
+  const uint32_t tid = threadIdx.x;
+  const uint32_t P = a.passes;
+  const uint32_t num_tiles = a.ctl->pad[0] ? 0u : a.ctl->num_tiles;
+  const K* keys = static_cast<const K*>(a.keys);
+  const K tc = (K)a.tw_c, tf = (K)a.tw_f;
+  Off* hist = static_cast<Off*>(a.seg_hist);
+  for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (uint32_t i = tid; i < P * kRadix; i += blockDim.x) s_cnt[i] = 0;
+    __syncthreads();
+    const uint32_t slot = a.tile_slot[t];
+    const SegRecord r = a.recs[slot];
+    const uint64_t off = (uint64_t)(t - r.tile_first) * a.tile;
+    const uint64_t base = r.begin + off;
+    const uint32_t valid = (uint32_t)((r.len - off) < (uint64_t)a.tile ? (r.len - off) : (uint64_t)a.tile);
+    for (uint32_t j = tid; j < valid; j += blockDim.x) {
+      const K tw = dev::twiddle_k<FK, K>(keys[base + j], tc, tf);
+      for (uint32_t p = 0; p < P; ++p) {
+        const uint32_t m = (p + 1 == P) ? a.last_mask : 0xffu;
+        atomicAdd(s_cnt + p * kRadix + ((uint32_t)(tw >> (a.begin_bit + 8 * p)) & m), 1u);
+      }
+    }
+    __syncthreads();
+    Off* h = hist + (size_t)slot * P * kRadix;
+    for (uint32_t i = tid; i < P * kRadix; i += blockDim.x)
+      if (s_cnt[i]) atomicAdd(h + i, (Off)s_cnt[i]);
+    __syncthreads();
+  }
+}
+
+// counts -> segment begin + exclusive digit prefix, per (slot, pass), in place
+template <typename Off>
+__global__ void __launch_bounds__(256) seg_scan_kernel(const SegHistArgs a) {
+  __shared__ Off s_part[8];
+  dev::pdl_wait();
+  dev::pdl_launch_dependents();
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t slots = a.ctl->pad[0] ? 0u : a.ctl->num_slots;
+  Off* hist = static_cast<Off*>(a.seg_hist);
+  for (uint64_t x = blockIdx.x; x < (uint64_t)slots * a.passes; x += gridDim.x) {
+    const uint64_t slot = x / a.passes;
+    Off* h = hist + x * kRadix;
+    const Off c = h[tid];
+    Off incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const Off t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= (uint32_t)o) incl += t;
+    }
+    if (lane == 31) s_part[warp] = incl;
+    __syncthreads();
+    Off pre = (Off)a.recs[slot].begin;
+    for (uint32_t w = 0; w < warp; ++w) pre += s_part[w];
+    h[tid] = pre + incl - c;
+    __syncthreads();
+  }
+}
+
+// begin_bit == end_bit: every segment is copied as it is
+template <int BYTES>
+__global__ void __launch_bounds__(256) seg_copy_kernel(const SegSmallArgs a) {
+  using T = typename dev::UIntOf<BYTES>::T;
+  (void)sizeof(T);
+  const T* in = static_cast<const T*>(a.keys_in);
+  T* out = static_cast<T*>(a.keys_out);
+  for (uint64_t s = blockIdx.x; s < a.num_segments; s += gridDim.x) {
+    const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
+    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) out[i] = in[i];
+  }
+}
+
+}  // namespace cusort_b200

@@ -82,4 +82,71 @@ struct OnesweepArgs {
   uint32_t tma_vals;
 };
 
+// Segmented sort: a segment longer than one small-sort block is cut into
+// onesweep tiles that never straddle segments.  One record per such segment
+// (index = its slot): first item, length, index of its first tile.
+struct SegRecord {
+  uint64_t begin;
+  uint64_t len;
+  uint32_t tile_first;
+  uint32_t pad;
+};
+
+// Planner output and counters of a segmented sort (device memory).
+struct SegControl {
+  uint32_t num_tiles;  // tiles of all multi-tile segments
+  uint32_t num_slots;  // multi-tile segments
+  uint32_t pad[2];
+};
+
+// Onesweep pass over the tiles of multi-tile segments: each tile's segment,
+// per-segment digit bases instead of one global histogram, and a lookback
+// that stops at the segment's first tile.
+struct SegOnesweepArgs : OnesweepArgs {
+  const SegRecord* recs;
+  const uint32_t* tile_slot;     // per tile: slot of its segment
+  const SegControl* ctl;         // num_tiles (written by the planner)
+  const void* seg_gbase;         // OffsetT[slot][passes][256]: segment begin + exclusive digit prefix
+  uint32_t seg_pass;             // index of this pass in seg_gbase
+  uint32_t seg_passes;
+};
+
+// Small-segment sorts and the planner.
+struct SegSmallArgs {
+  const void* keys_in;
+  void* keys_out;
+  const void* vals_in;
+  void* vals_out;
+  const int64_t* begin_offsets;
+  const int64_t* end_offsets;
+  uint64_t num_segments;
+  uint64_t min_len, max_len;     // this kernel sorts segments with min_len <= len <= max_len
+  uint64_t tw_c, tw_f;
+  uint32_t begin_bit, passes, last_mask;
+  uint32_t pad;
+};
+
+struct SegPlanArgs {
+  const int64_t* begin_offsets;
+  const int64_t* end_offsets;
+  uint64_t num_segments;
+  uint64_t min_len;              // segments longer than this are tiled
+  uint32_t tile;                 // items per onesweep tile
+  uint32_t max_slots, max_tiles; // capacity of recs / tile_slot (bounds-checked)
+  SegRecord* recs;
+  uint32_t* tile_slot;
+  SegControl* ctl;
+  uint32_t* status;
+};
+
+struct SegHistArgs {
+  const void* keys;
+  const SegRecord* recs;
+  const uint32_t* tile_slot;
+  const SegControl* ctl;
+  void* seg_hist;                // OffsetT[slot][passes][256], zeroed; scanned in place by seg_scan
+  uint64_t tw_c, tw_f;
+  uint32_t tile, begin_bit, passes, last_mask;
+};
+
 }  // namespace cusort_b200

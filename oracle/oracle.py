@@ -7,6 +7,12 @@ bench.py's cpu_baseline / reference legs -- never by the libcusort_b200 product.
   masked twiddled key; libcusort.cuh semantics cited there.
 * ``numpy_sort``: an independent numpy restatement (np.argsort kind="stable"),
   used to cross-check the C++ oracle.
+* ``oracle_segmented_sort`` / ``numpy_segmented_sort``: the segmented sort's
+  semantics (each segment [begin, end) sorted independently and stably in
+  place of the output, everything else untouched), over the C++ oracle per
+  segment and over one numpy lexsort by (segment, digit key) respectively.
+  The reference has no segmented sort (only the name, libcusort.cuh:4); the
+  semantics follow CUB's DeviceSegmentedRadixSort.
 * ``ref_sort``: the UNMODIFIED reference, compiled for sm_100a into
   oracle/_ref/libcusort_ref.so by oracle/Makefile (needs a GPU to run).
 """
@@ -137,6 +143,46 @@ def numpy_sort(kt: str, keys: np.ndarray, values=None, begin_bit=0, end_bit=None
     dk = numpy_digit_keys(kt, keys, begin_bit, end_bit, descending)
     perm = np.argsort(dk, kind="stable")
     return keys[perm], (None if values is None else values[perm])
+
+
+def oracle_segmented_sort(kt: str, keys: np.ndarray, values, begins, ends, begin_bit: int = 0,
+                          end_bit: int | None = None, descending: bool = False, keys_out=None, values_out=None):
+    """Segmented stable sort: out[b:e] = oracle_sort(keys[b:e]) per segment; other positions keep
+    keys_out / values_out (copied) as given."""
+    ko = np.array(keys_out if keys_out is not None else np.zeros_like(keys), copy=True)
+    vo = None
+    if values is not None:
+        vo = np.array(values_out if values_out is not None else np.zeros_like(values), copy=True)
+    for b, e in zip(np.asarray(begins).tolist(), np.asarray(ends).tolist()):
+        if e <= b:
+            continue
+        k, v = oracle_sort(kt, keys[b:e], None if values is None else values[b:e], begin_bit, end_bit, descending)
+        ko[b:e] = k
+        if values is not None:
+            vo[b:e] = v
+    return ko, vo
+
+
+def numpy_segmented_sort(kt: str, keys: np.ndarray, values, begins, ends, begin_bit: int = 0,
+                         end_bit: int | None = None, descending: bool = False, keys_out=None, values_out=None):
+    """Independent restatement: one stable lexsort of the in-segment items by (segment, digit key)."""
+    end_bit = 8 * keys.dtype.itemsize if end_bit is None else end_bit
+    ko = np.array(keys_out if keys_out is not None else np.zeros_like(keys), copy=True)
+    vo = None if values is None else np.array(values_out if values_out is not None else np.zeros_like(values),
+                                                copy=True)
+    begins = np.asarray(begins, dtype=np.int64)
+    ends = np.asarray(ends, dtype=np.int64)
+    lens = np.maximum(ends - begins, 0)
+    if lens.sum() == 0:
+        return ko, vo
+    seg = np.repeat(np.arange(len(begins)), lens)
+    pos = np.concatenate([np.arange(b, b + m) for b, m in zip(begins.tolist(), lens.tolist()) if m > 0])
+    dk = numpy_digit_keys(kt, keys[pos], begin_bit, end_bit, descending)
+    order = np.lexsort((dk, seg))  # stable: ties keep the in-segment input order
+    ko[pos] = keys[pos[order]]
+    if values is not None:
+        vo[pos] = values[pos[order]]
+    return ko, vo
 
 
 # ---------------------------------------------------------------------------
