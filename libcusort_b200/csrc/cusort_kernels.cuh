@@ -605,16 +605,16 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 
   // A tile is staged by TMA when it is full and both inputs are 16-byte aligned.
   auto tma_tile = [&](uint32_t t) {
-    if constexpr (CFG::SEG) return false;  // segment tiles start anywhere: cooperative loads
+    if constexpr (CFG::SEG) return false;  // per tile, below (segment tiles start anywhere)
     return !CFG::DIRECT_LOAD && tma_ok && t < num_tiles && (uint64_t)(t + 1) * TILE <= a.n;
   };
-  auto issue_tma = [&](uint32_t t, int buf) {
-    const uint64_t base = (uint64_t)t * TILE;
+  auto issue_tma_at = [&](uint64_t base, int buf) {
     uint8_t* bp = smem + (size_t)buf * CFG::BUF_BYTES;
     dev::mbar_arrive_expect_tx(s_mbar + buf, (uint32_t)TILE * (CFG::KB + CFG::VB));
     dev::tma_load_1d(bp, keys_in + base, (uint32_t)TILE * CFG::KB, s_mbar + buf, pol);
     if constexpr (HAS_V) dev::tma_load_1d(bp + CFG::KEYS_BYTES, vals_in + base, (uint32_t)TILE * CFG::VB, s_mbar + buf, pol);
   };
+  auto issue_tma = [&](uint32_t t, int buf) { issue_tma_at((uint64_t)t * TILE, buf); };
   // Bounded wait for a buffer's bulk copy; false if it timed out.
   auto wait_tma = [&](int buf, uint32_t parity) {
     dev::SpinGuard guard;
@@ -636,8 +636,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   // Global exclusive offset of every digit for this pass (from the upfront
   // histogram), computed once per CTA; the first tile ticket is taken here.
   if constexpr (CFG::SEG) {
-    // per-segment digit bases are loaded per tile
-    num_tiles = a.ctl->num_tiles;
+    // per-segment digit bases are loaded per tile; nothing to do after a
+    // planner overflow (overlapping segments)
+    num_tiles = a.ctl->pad[0] ? 0u : a.ctl->num_tiles;
     if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
     __syncthreads();
   } else if constexpr (CFG::ROUTED) {
@@ -739,8 +740,15 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     V* s_vals = reinterpret_cast<V*>(smem + (size_t)b * CFG::BUF_BYTES + CFG::KEYS_BYTES);
 
     // ---- 1. the tile's keys/values in shared memory
-    if (tma_tile(tile)) {
-      if (NBUF == 1 && tid == 0) issue_tma(tile, 0);
+    bool use_tma = tma_tile(tile);
+    if constexpr (CFG::SEG) {
+      // a full tile whose start is 16-byte aligned in both inputs
+      use_tma = !CFG::DIRECT_LOAD && NBUF == 1 && tma_ok && valid == (uint32_t)TILE &&
+                ((reinterpret_cast<uintptr_t>(keys_in + base) | (HAS_V ? reinterpret_cast<uintptr_t>(vals_in + base)
+                                                                       : uintptr_t(0))) & 15u) == 0;
+    }
+    if (use_tma) {
+      if (NBUF == 1 && tid == 0) issue_tma_at(base, 0);
       const bool ok = wait_tma(b, (parity >> b) & 1u);
       parity ^= 1u << b;
       if (!ok) {

@@ -176,6 +176,8 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
   const int seg_grid = (int)std::min<int64_t>(num_segments, 1 << 20);
 
   if (P == 0) {  // zero-width key range: every segment copied as it is
+    cudaError_t z = cudaMemsetAsync(d_temp, 0, 256, stream);  // status word
+    if (z) return z;
     SegSmallArgs c = {};
     c.keys_in = kin;
     c.keys_out = kout;
@@ -293,8 +295,10 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
       a.status = status;
       a.spin_limit_ns = wait_limit_ns();
       a.skip_tile = -1;
-      a.tma_keys = 0;
-      a.tma_vals = 0;
+      // TMA tile loads where a tile starts 16-byte aligned (checked per tile)
+      const size_t tile_k = (size_t)k.onesweep.tile * kb, tile_v = (size_t)k.onesweep.tile * vb;
+      a.tma_keys = (tile_k & 15) == 0 ? 1u : 0u;
+      a.tma_vals = (vb == 0 || (tile_v & 15) == 0) ? 1u : 0u;
       a.recs = reinterpret_cast<const SegRecord*>(t + L.recs);
       a.tile_slot = reinterpret_cast<const uint32_t*>(t + L.tile_slot);
       a.ctl = ctl;

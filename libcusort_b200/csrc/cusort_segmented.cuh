@@ -99,8 +99,12 @@ __global__ void __launch_bounds__(256) seg_small_kernel(const SegSmallArgs a) {
       V val[HAS_V ? KPT : 1];
       uint32_t rd[KPT];  // digit (9 bits, 0x100 = past the end) | rank within the warp << 9
       const uint32_t wfirst = wg * KPT * 32;
+      // slots past the segment's end (warp-uniform) are skipped: short
+      // segments cost their own length, not the group's capacity
 #pragma unroll
       for (int sl = 0; sl < KPT; ++sl) {
+        rd[sl] = 0x100u;
+        if (wfirst + sl * 32 >= n) continue;
         const uint32_t i = wfirst + sl * 32 + lane;
         const bool in = i < n;
         key[sl] = in ? sk[i] : K(0);
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(256) seg_small_kernel(const SegSmallArgs a) {
 #pragma unroll
       for (int sl = 0; sl < KPT; ++sl) {
         const uint32_t d = rd[sl] & 0x1ffu;
-        if (d < kRadix) {
+        if (d < kRadix) {  // 0x100: past the end
           const uint32_t pos = cnt[wg * kRadix + d] + (rd[sl] >> 9);
           sk[pos] = key[sl];
           if constexpr (HAS_V) sv[pos] = val[sl];
@@ -191,10 +195,28 @@ __global__ void __launch_bounds__(512) seg_hist_kernel(const SegHistArgs a) {
   const K* keys = static_cast<const K*>(a.keys);
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
   Off* hist = static_cast<Off*>(a.seg_hist);
-  for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-    for (uint32_t i = tid; i < P * kRadix; i += blockDim.x) s_cnt[i] = 0;
+  // Each CTA counts a contiguous range of tiles and flushes its counts when
+  // the segment changes (and at the end), so a long segment costs one flush
+  // per CTA, not one per tile.
+  const uint32_t per = (num_tiles + gridDim.x - 1) / gridDim.x;
+  const uint32_t t0 = blockIdx.x * per, t1 = min(num_tiles, t0 + per);
+  for (uint32_t i = tid; i < P * kRadix; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  uint32_t cur_slot = 0xffffffffu;
+  auto flush = [&]() {
+    Off* h = hist + (size_t)cur_slot * P * kRadix;
+    for (uint32_t i = tid; i < P * kRadix; i += blockDim.x) {
+      if (s_cnt[i]) atomicAdd(h + i, (Off)s_cnt[i]);
+      s_cnt[i] = 0;
+    }
     __syncthreads();
+  };
+  for (uint32_t t = t0; t < t1; ++t) {
     const uint32_t slot = a.tile_slot[t];
+    if (slot != cur_slot) {
+      if (cur_slot != 0xffffffffu) flush();
+      cur_slot = slot;
+    }
     const SegRecord r = a.recs[slot];
     const uint64_t off = (uint64_t)(t - r.tile_first) * a.tile;
     const uint64_t base = r.begin + off;
@@ -207,11 +229,8 @@ __global__ void __launch_bounds__(512) seg_hist_kernel(const SegHistArgs a) {
       }
     }
     __syncthreads();
-    Off* h = hist + (size_t)slot * P * kRadix;
-    for (uint32_t i = tid; i < P * kRadix; i += blockDim.x)
-      if (s_cnt[i]) atomicAdd(h + i, (Off)s_cnt[i]);
-    __syncthreads();
   }
+  if (cur_slot != 0xffffffffu) flush();
 }
 
 // counts -> segment begin + exclusive digit prefix, per (slot, pass), in place

