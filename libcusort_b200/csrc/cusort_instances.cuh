@@ -39,14 +39,27 @@ namespace cusort_b200 {
 #define CUSORT_OS_KPT_GT16 8
 #endif
 
+// 8-byte keys with 8- or 16-byte values: smaller tiles than the byte-size
+// rule, which would spill registers (measured on B200, 2^26 items: u64 + 16 B
+// 8.07 -> 6.67 ms at KPT 6, u64 + 8 B 5.83 -> 4.66 ms at KPT 10; the other
+// shapes were equal or slower with smaller tiles).
+#ifndef CUSORT_OS_KPT_K8V16
+#define CUSORT_OS_KPT_K8V16 6
+#endif
+#ifndef CUSORT_OS_KPT_K8V8
+#define CUSORT_OS_KPT_K8V8 10
+#endif
+
 template <int KB, int VB>
 struct TileShape {
   static constexpr int THREADS = CUSORT_OS_THREADS;
   static constexpr int BYTES = KB + VB;
-  static constexpr int KPT = (VB == 0 && KB <= 4) ? CUSORT_OS_KPT_KEYS4
-                             : (BYTES > 16)       ? CUSORT_OS_KPT_GT16
-                             : (BYTES > 8)        ? CUSORT_OS_KPT_LE16
-                                                  : CUSORT_OS_KPT_LE8;
+  static constexpr int KPT = (KB == 8 && VB == 16)  ? CUSORT_OS_KPT_K8V16
+                             : (KB == 8 && VB == 8) ? CUSORT_OS_KPT_K8V8
+                             : (VB == 0 && KB <= 4) ? CUSORT_OS_KPT_KEYS4
+                             : (BYTES > 16)         ? CUSORT_OS_KPT_GT16
+                             : (BYTES > 8)          ? CUSORT_OS_KPT_LE16
+                                                    : CUSORT_OS_KPT_LE8;
   static constexpr int MINB = CUSORT_OS_MINB;
 };
 

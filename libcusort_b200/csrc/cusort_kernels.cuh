@@ -516,7 +516,12 @@ struct OnesweepCfg {
   static_assert(TILE <= 65536, "16-bit tile positions");
 };
 
-constexpr int kLookbackWindow = 8;
+// Predecessor words read per lookback round trip: 8 with 32-bit words; 4 with
+// 64-bit words (n >= 2^30), where 8 would make the pass spill registers.
+template <typename Off>
+constexpr int lookback_window() {
+  return sizeof(Off) == 8 ? 4 : 8;
+}
 
 template <typename Off>
 struct DescBits {
@@ -890,7 +895,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     if (tid < kRadix) {
       Off excl = 0;
       if (tile > floor) {
-        excl = lookback_prefix<Off, kLookbackWindow>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, floor);
+        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, floor);
         if (publish)
           dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
       }
