@@ -567,7 +567,7 @@ cudaError_t digit_counts_u64(int kt, bool desc, const void* keys, int64_t n, int
 
 cudaError_t routed_partition(int kt, size_t vb, bool desc, const void* keys, const void* vals, int64_t n,
                              int begin_bit, int end_bit, bool wide_offsets, const RouteTable* d_route, void* d_temp,
-                             size_t* temp_bytes, cudaStream_t stream) {
+                             size_t* temp_bytes, cudaStream_t stream, bool keep_status) {
   const int kb = key_bytes_of(kt);
   if (kb == 0 || temp_bytes == nullptr || n < 0) return cudaErrorInvalidValue;
   if (vb != 0 && !value_bytes_ok(vb)) return cudaErrorInvalidValue;
@@ -603,12 +603,15 @@ cudaError_t routed_partition(int kt, size_t vb, bool desc, const void* keys, con
   Launch& li = ls[0];
   li = Launch{};
   li.func = get_init_kernel();
-  const uint64_t n16 = need / 16;
+  // keep_status: the status word (first 16 bytes) keeps the bits of earlier
+  // passes that used this temp storage
+  const uint64_t skip16 = keep_status ? 1 : 0;
+  const uint64_t n16 = need / 16 - skip16;
   li.grid = (int)std::min<uint64_t>((uint64_t)sms * 4, std::max<uint64_t>(1, (n16 + 511) / 512));
   li.threads = 512;
   li.pdl = false;
   li.kind = 0;
-  li.args.init.ptr = d_temp;
+  li.args.init.ptr = t + 16 * skip16;
   li.args.init.n16 = n16;
   Launch& l = ls[1];
   l = Launch{};

@@ -62,9 +62,11 @@ struct RouteTable;
 // route->base[d] + (rank of the item among this call's items of digit d):
 // the fused partition + exchange of the multi-GPU sort.  `d_route` is device
 // memory.  wide_offsets selects 64-bit offsets (destinations >= 2^32 items).
-// With d_temp == nullptr only *temp_bytes is set (cusort_api.cu).
+// With d_temp == nullptr only *temp_bytes is set (cusort_api.cu).  keep_status
+// leaves the status word of d_temp as earlier passes left it.
 cudaError_t routed_partition(int key_type, size_t value_bytes, bool descending, const void* keys, const void* values,
                              int64_t num_items, int begin_bit, int end_bit, bool wide_offsets,
-                             const RouteTable* d_route, void* d_temp, size_t* temp_bytes, cudaStream_t stream);
+                             const RouteTable* d_route, void* d_temp, size_t* temp_bytes, cudaStream_t stream,
+                             bool keep_status = false);
 
 }  // namespace cusort_b200

@@ -16,7 +16,12 @@
 //      over NVLink (peer buffers mapped once through CUDA IPC), tiles in
 //      order after the runs of lower source ranks.  Long runs keep the
 //      remote stores efficient.  A one-word ncclAllReduce then fences the
-//      exchange.  Fallbacks, chosen when a rank cannot map its buffers (or by
+//      exchange.  CUSORT_MGPU_EXCHANGE=pipe runs the routed pass chunk by
+//      chunk (up to 8 chunks of >= 2^24 items), this rank's own items straight
+//      into its receive buffer and each peer's into one contiguous staging run
+//      per chunk, which the copy engines push into the peer's buffer while the
+//      next chunk is partitioned (measured equal to "routed" at 2 GPUs).
+//      Fallbacks, chosen when a rank cannot map its buffers (or by
 //      CUSORT_MGPU_EXCHANGE=copy|nccl): a local partition pass, then
 //      copy-engine pushes into the mapped peer buffers ("copy") or grouped
 //      ncclSend/ncclRecv ("nccl"), pieces laid out by source rank;
@@ -79,10 +84,51 @@ thread_local PinnedCounts g_pinned_counts;
 struct MgpuComm {
   ncclComm_t nccl = nullptr;
   std::map<std::pair<int, std::string>, void*> mapped;  // (peer, IPC handle) -> local address
+  // pipelined exchange: copy streams (one per peer, up to kMaxCopyStreams) and events
+  std::vector<cudaStream_t> copy_streams;
+  std::vector<cudaEvent_t> events;
+  ~MgpuComm() {
+    for (cudaStream_t s : copy_streams) cudaStreamDestroy(s);
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+  }
 };
 
 // Exchange modes, ordered: the call uses the lowest mode any rank asks for.
-enum : unsigned long long { kXchgNccl = 0, kXchgCopy = 1, kXchgRouted = 2 };
+enum : unsigned long long { kXchgNccl = 0, kXchgCopy = 1, kXchgRouted = 2, kXchgPipe = 3 };
+
+// Pipelined exchange: the local slice is partitioned in chunks of at least
+// 2^24 items (at most kMaxChunks); chunk c's pieces for peers are copied by
+// the copy engines while chunk c+1 is partitioned.
+constexpr int kMaxChunks = 8;
+constexpr int kMaxCopyStreams = 8;
+int chunks_for(int64_t n_local) {
+  const char* force = std::getenv("CUSORT_MGPU_CHUNKS");  // tests: pipeline small inputs too
+  if (force && std::atoi(force) >= 1)
+    return (int)std::min<int64_t>(std::min(kMaxChunks, std::atoi(force)), std::max<int64_t>(1, n_local));
+  return (int)std::min<int64_t>(kMaxChunks, std::max<int64_t>(1, n_local >> 24));
+}
+
+__global__ void sum_chunk_counts_kernel(const unsigned long long* chunk_counts, int chunks, unsigned long long* out) {
+  unsigned long long s = 0;
+  for (int c = 0; c < chunks; ++c) s += chunk_counts[c * 256 + threadIdx.x];
+  out[threadIdx.x] = s;
+}
+
+cudaError_t comm_resources(MgpuComm* mc, int streams, int events) {
+  while ((int)mc->copy_streams.size() < streams) {
+    cudaStream_t s;
+    cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e) return e;
+    mc->copy_streams.push_back(s);
+  }
+  while ((int)mc->events.size() < events) {
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e) return e;
+    mc->events.push_back(ev);
+  }
+  return cudaSuccess;
+}
 
 // Per-rank record all-gathered before the exchange.
 struct RankRecord {
@@ -183,8 +229,8 @@ cudaError_t nccl_to_cuda(ncclResult_t r) {
 }
 
 struct MgpuLayout {
-  size_t route_tmp, route_tmp_bytes, route, counts, all_counts, part_k, part_v, alt_k, alt_v, sort_tmp,
-      sort_tmp_bytes, total;
+  size_t route_tmp, route_tmp_bytes, route, chunk_counts, counts, all_counts, part_k, part_v, alt_k, alt_v,
+      sort_tmp, sort_tmp_bytes, total;
 };
 
 // Temp storage of one call; the local sorts' sizes come from this library's
@@ -230,8 +276,10 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
   L->route_tmp = o;  // first, so that the status word at d_temp is the routed pass's
   L->route_tmp_bytes = route_tmp;
   o += a256(route_tmp);
-  L->route = o;
-  o += a256(sizeof(cusort_b200::RouteTable));
+  L->route = o;  // one route table per chunk
+  o += a256(kMaxChunks * sizeof(cusort_b200::RouteTable));
+  L->chunk_counts = o;
+  o += a256((size_t)kMaxChunks * 256 * sizeof(unsigned long long));
   L->counts = o;  // this rank's RankRecord (counts first), then the fence word
   o += a256(sizeof(RankRecord) + 16);
   L->all_counts = o;  // every rank's RankRecord
@@ -325,6 +373,7 @@ cudaError_t cusort_mgpu_comm_destroy(void* comm) {
   if (!comm) return cudaErrorInvalidValue;
   MgpuComm* mc = static_cast<MgpuComm*>(comm);
   for (auto& kv : mc->mapped) cudaIpcCloseMemHandle(kv.second);
+  for (cudaStream_t st : mc->copy_streams) cudaStreamSynchronize(st);
   const cudaError_t e = nccl_to_cuda(ncclCommDestroy(mc->nccl));
   delete mc;
   return e;
@@ -413,23 +462,42 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   RankRecord* rec = reinterpret_cast<RankRecord*>(t + L.counts);
   RankRecord* all_rec = reinterpret_cast<RankRecord*>(t + L.all_counts);
   int* fence = reinterpret_cast<int*>(t + L.counts + sizeof(RankRecord));
-  e = cusort_b200::digit_counts_u64(kt, desc, d_keys_in, n_local, msd_begin, end_bit, rec->counts, stream);
+  // CUSORT_MGPU_EXCHANGE=pipe|copy|nccl selects another exchange than the
+  // routed pass (the mode is all-gathered, so every rank takes the same path).
+  const char* ex = std::getenv("CUSORT_MGPU_EXCHANGE");
+  unsigned long long want = kXchgRouted;
+  if (ex && std::strcmp(ex, "pipe") == 0) want = kXchgPipe;
+  if (ex && std::strcmp(ex, "copy") == 0) want = kXchgCopy;
+  if (ex && std::strcmp(ex, "nccl") == 0) want = kXchgNccl;
+  const int chunks = chunks_for(n_local);
+  if (want == kXchgPipe && chunks == 1) want = kXchgRouted;  // nothing to overlap
+  if (want >= kXchgRouted && nranks > cusort_b200::kMaxRouteRanks) want = kXchgCopy;
+  const int64_t chunk_items = (n_local + chunks - 1) / chunks;
+  unsigned long long* d_cc = reinterpret_cast<unsigned long long*>(t + L.chunk_counts);
+  if (want == kXchgPipe) {
+    // per-chunk digit counts, and their sum for the record
+    for (int c = 0; c < chunks && !e; ++c) {
+      const int64_t c0 = c * chunk_items, cn = std::max<int64_t>(0, std::min(n_local - c0, chunk_items));
+      e = cusort_b200::digit_counts_u64(kt, desc, static_cast<const uint8_t*>(d_keys_in) + c0 * kb, cn, msd_begin,
+                                        end_bit, d_cc + c * 256, stream);
+    }
+    if (e) return e;
+    sum_chunk_counts_kernel<<<1, 256, 0, stream>>>(d_cc, chunks, rec->counts);
+    e = cudaGetLastError();
+  } else {
+    e = cusort_b200::digit_counts_u64(kt, desc, d_keys_in, n_local, msd_begin, end_bit, rec->counts, stream);
+  }
   if (e) return e;
   const size_t tail = sizeof(RankRecord) - offsetof(RankRecord, hk);
-  e = g_pinned_counts.reserve(((size_t)nranks * sizeof(RankRecord) + tail) / 8 + 1);
+  const size_t rec_words = ((size_t)nranks * sizeof(RankRecord) + tail + 7) / 8;
+  e = g_pinned_counts.reserve(rec_words + (size_t)kMaxChunks * 256);
   if (e) return e;
   RankRecord* h_all = reinterpret_cast<RankRecord*>(g_pinned_counts.p);
   uint8_t* h_tail = reinterpret_cast<uint8_t*>(h_all + nranks);
+  unsigned long long* h_cc = reinterpret_cast<unsigned long long*>(g_pinned_counts.p + rec_words);
   unsigned long long my_mode = kXchgNccl;
   {
     RankRecord mine;
-    // CUSORT_MGPU_EXCHANGE=copy|nccl selects a fallback exchange (the mode is
-    // all-gathered, so every rank takes the same path).
-    const char* ex = std::getenv("CUSORT_MGPU_EXCHANGE");
-    unsigned long long want = kXchgRouted;
-    if (ex && std::strcmp(ex, "nccl") == 0) want = kXchgNccl;
-    if (ex && std::strcmp(ex, "copy") == 0) want = kXchgCopy;
-    if (want == kXchgRouted && nranks > cusort_b200::kMaxRouteRanks) want = kXchgCopy;
     const bool ok = want != kXchgNccl && export_buffer(rk, &mine.hk, &mine.off_k) &&
                     (vb == 0 || export_buffer(rv, &mine.hv, &mine.off_v));
     if (vb == 0) {
@@ -448,6 +516,11 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   if (e) return e;
   e = cudaMemcpyAsync(h_all, all_rec, (size_t)nranks * sizeof(RankRecord), cudaMemcpyDeviceToHost, stream);
   if (e) return e;
+  if (want == kXchgPipe) {
+    e = cudaMemcpyAsync(h_cc, d_cc, (size_t)chunks * 256 * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                        stream);
+    if (e) return e;
+  }
   cudaEvent_t counts_ready;
   e = cudaEventCreateWithFlags(&counts_ready, cudaEventDisableTiming);
   if (e) return e;
@@ -459,7 +532,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   timer.mark("counts+gather");
 
   // 4 (fallback modes). stable partition by the owner digit into part_k/v.
-  //    Unless this rank asked for the routed exchange, it is enqueued before
+  //    When this rank asked for a fallback exchange, it is enqueued before
   //    the host waits for the records, so the host round trip overlaps this
   //    pass.  (It does not depend on the plan: owners are contiguous digit
   //    ranges.)
@@ -477,7 +550,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
                                    stream);
   };
   bool partitioned = false;
-  if (my_mode != kXchgRouted) {
+  if (my_mode == kXchgCopy || my_mode == kXchgNccl) {
     e = partition();
     if (e) {
       cudaEventDestroy(counts_ready);
@@ -506,7 +579,103 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
 
   // 5. all-to-all
   timer.mark("host");
-  if (mode == kXchgRouted) {
+  if (mode == kXchgPipe) {
+    // Pipelined: chunk c is partitioned by the routed pass -- this rank's own
+    // items straight into its receive buffer, each peer's into one staging
+    // run -- and the copy engines push chunk c's staging runs into the peers'
+    // receive buffers while chunk c+1 is partitioned.  Peer q's buffer gets
+    // this rank's chunks in order after the items of lower source ranks.
+    const int peers = nranks - 1;
+    const int ns = std::min(peers, kMaxCopyStreams);
+    e = comm_resources(mc, ns, chunks + ns);
+    if (e) return e;
+    std::vector<int64_t> cnt((size_t)chunks * nranks, 0);  // [c][q]
+    for (int c = 0; c < chunks; ++c)
+      for (int d = 0; d < 256; ++d) cnt[(size_t)c * nranks + owner[d]] += (int64_t)h_cc[c * 256 + d];
+    std::vector<int64_t> at((size_t)nranks, 0);  // this rank's offset in q's buffer
+    for (int q = 0; q < nranks; ++q)
+      for (int p = 0; p < rank; ++p)
+        for (int d = 0; d < 256; ++d)
+          if (owner[d] == q) at[q] += (int64_t)all_counts[(size_t)p * 256 + d];
+    std::vector<uint8_t*> pk((size_t)nranks, nullptr), pv((size_t)nranks, nullptr);
+    for (int q = 0; q < nranks && !e; ++q) {
+      if (q == rank) continue;
+      e = peer_address(mc, q, h_all[q].hk, h_all[q].off_k, &pk[q]);
+      if (!e && vb) e = peer_address(mc, q, h_all[q].hv, h_all[q].off_v, &pv[q]);
+    }
+    if (e) return e;
+    std::vector<cusort_b200::RouteTable> rts((size_t)chunks);
+    std::vector<int64_t> stage((size_t)chunks * nranks, 0), dst((size_t)chunks * nranks, 0);
+    int64_t so = 0;
+    std::vector<int64_t> run = at;  // next free offset per destination
+    for (int c = 0; c < chunks; ++c) {
+      cusort_b200::RouteTable& rt = rts[c];
+      std::memset(&rt, 0, sizeof(rt));
+      for (int d = 255; d >= 0; --d) {
+        rt.owner[d] = (unsigned char)owner[d];
+        rt.first_digit[owner[d]] = (unsigned int)d;
+      }
+      for (int d = 0; d < 256; ++d) rt.last_digit[owner[d]] = (unsigned int)d;
+      for (int q = 0; q < nranks; ++q) {
+        const int64_t m = cnt[(size_t)c * nranks + q];
+        dst[(size_t)c * nranks + q] = run[q];
+        if (q == rank) {
+          rt.kptr[q] = reinterpret_cast<unsigned long long>(rk);
+          rt.vptr[q] = vb ? reinterpret_cast<unsigned long long>(rv) : 0ull;
+          rt.cap[q] = (unsigned long long)out_capacity;
+          rt.base[q] = (unsigned long long)run[q];
+        } else {
+          rt.kptr[q] = reinterpret_cast<unsigned long long>(part_k);
+          rt.vptr[q] = vb ? reinterpret_cast<unsigned long long>(part_v) : 0ull;
+          rt.cap[q] = (unsigned long long)n_local;
+          rt.base[q] = (unsigned long long)so;
+          stage[(size_t)c * nranks + q] = so;
+          so += m;
+        }
+        run[q] += m;
+      }
+    }
+    const bool wide = (uint64_t)out_capacity > 0xFFFFFFFFull || (uint64_t)n_local > 0xFFFFFFFFull;
+    auto* d_rt = reinterpret_cast<cusort_b200::RouteTable*>(t + L.route);
+    // pageable source: staged before the call returns; the stream is idle here
+    e = cudaMemcpyAsync(d_rt, rts.data(), (size_t)chunks * sizeof(cusort_b200::RouteTable), cudaMemcpyHostToDevice,
+                        stream);
+    if (e) return e;
+    std::vector<bool> used((size_t)ns, false);
+    for (int c = 0; c < chunks && !e; ++c) {
+      const int64_t c0 = c * chunk_items, cn = std::max<int64_t>(0, std::min(n_local - c0, chunk_items));
+      size_t rtb = L.route_tmp_bytes;
+      e = cusort_b200::routed_partition(kt, vb, desc, static_cast<const uint8_t*>(d_keys_in) + c0 * kb,
+                                        vb ? static_cast<const uint8_t*>(d_values_in) + c0 * vb : nullptr, cn,
+                                        msd_begin, end_bit, wide, d_rt + c, t + L.route_tmp, &rtb, stream, c > 0);
+      if (!e) e = cudaEventRecord(mc->events[c], stream);
+      for (int q = 0; q < nranks && !e; ++q) {
+        const int64_t m = cnt[(size_t)c * nranks + q];
+        if (q == rank || m == 0) continue;
+        const int j = (q < rank ? q : q - 1) % ns;
+        cudaStream_t cs = mc->copy_streams[j];
+        e = cudaStreamWaitEvent(cs, mc->events[c], 0);
+        used[j] = true;
+        const int64_t sidx = stage[(size_t)c * nranks + q], didx = dst[(size_t)c * nranks + q];
+        if (!e)
+          e = cudaMemcpyAsync(pk[q] + didx * kb, static_cast<uint8_t*>(part_k) + sidx * kb, (size_t)m * kb,
+                              cudaMemcpyDeviceToDevice, cs);
+        if (!e && vb)
+          e = cudaMemcpyAsync(pv[q] + didx * vb, static_cast<uint8_t*>(part_v) + sidx * vb, (size_t)m * vb,
+                              cudaMemcpyDeviceToDevice, cs);
+      }
+    }
+    // join the copy streams, then fence
+    for (int j = 0; j < ns && !e; ++j) {
+      if (!used[j]) continue;
+      e = cudaEventRecord(mc->events[chunks + j], mc->copy_streams[j]);
+      if (!e) e = cudaStreamWaitEvent(stream, mc->events[chunks + j], 0);
+    }
+    timer.mark("routed-pass");
+    if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
+    if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
+    if (e) return e;
+  } else if (mode == kXchgRouted) {
     // Fused partition + exchange: this rank's items for q go after the items
     // q receives from lower source ranks, tile by tile.
     cusort_b200::RouteTable rt;

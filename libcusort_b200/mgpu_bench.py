@@ -26,6 +26,9 @@ def _peaks(root: Path):
 
 
 _XCHG_DESC = {
+    "pipe": "MSD-digit all-gather, chunked fused partition pass (own items straight into this GPU's receive buffer, "
+            "each peer's into a contiguous staging run) with copy-engine pushes into the peers' IPC-mapped buffers "
+            "overlapping the next chunk, NCCL one-word fence, local sort",
     "routed": "MSD-digit all-gather, ONE fused partition+exchange onesweep pass storing each item into its "
               "owner's buffer over NVLink (IPC-mapped peer pointers), NCCL one-word fence, local sort",
     "copy": "MSD-digit all-gather, partition pass, all-to-all as copy-engine pushes over NVLink into "
@@ -33,8 +36,13 @@ _XCHG_DESC = {
     "nccl": "MSD-digit all-gather, partition pass, all-to-all as grouped ncclSend/ncclRecv, local sort",
 }
 # Library kernels per step: digit count (1) + partition (routed: init + onesweep = 2; otherwise
-# init + histogram + onesweep = 3) + local 4-pass sort (init + histogram + 4 onesweep = 6).
+# init + histogram + onesweep = 3) + local 4-pass sort (init + histogram + 4 onesweep = 6); the
+# pipelined exchange runs C chunks: C digit counts + 1 sum + C x (init + onesweep) + 6.
 _LAUNCHES = {"routed": 9, "copy": 10, "nccl": 10}
+
+
+def _chunks(n_local: int) -> int:
+    return min(8, max(1, n_local >> 24))
 
 
 def run(args, torch):
@@ -162,6 +170,9 @@ def run(args, torch):
             return None
         mode = os.environ.get("CUSORT_MGPU_EXCHANGE", "routed")
         mode = mode if mode in _XCHG_DESC else "routed"
+        if mode == "pipe" and _chunks(n_local) == 1:
+            mode = "routed"
+        launches = (3 * _chunks(n_local) + 7) if mode == "pipe" else _LAUNCHES[mode]
         root = Path(__file__).resolve().parents[1]
         peak, peak_src = _peaks(root)
         kb = vb = 4
@@ -180,7 +191,7 @@ def run(args, torch):
                        "n_total": n_total, "n_per_gpu": n_local, "parallelism": f"shard{world}",
                        "l2": f"inputs per GPU {n_local * 8 / 2**20:.0f} MiB > L2"},
             "verified": {"ranks_sorted": sorted_ok, "ranks_ordered": order_ok, "counts": counts_ok},
-            "gpu_launches": args.steps * _LAUNCHES[mode],
+            "gpu_launches": args.steps * launches,
             "roofline": {"bound": "hbm+nvlink", "achieved_frac_of_pipeline": t_ideal / (ms_step * 1e-3),
                          "t_ideal_ms": t_ideal * 1e3, "local_hbm_bytes_per_gpu": local_bytes,
                          "nvlink_bytes_per_gpu": xchg, "peak_hbm_gbs": peak, "peak_source": peak_src,

@@ -4,8 +4,10 @@ With one GPU: a 1-rank communicator must give the single-GPU result.  With
 >= 2 GPUs (one process per GPU, NCCL): the ranks' concatenated outputs must
 equal the CPU oracle's stable sort of the global input, bit-exact, for each
 exchange mode -- the fused partition + exchange pass writing into peers'
-buffers ("routed", the default), copy-engine pushes ("copy") and NCCL
-send/recv ("nccl") -- on two calls in a row with different inputs.
+buffers ("routed", the default), the same pass run in chunks with copy-engine
+pushes overlapping it ("pipe"; forced to 3 chunks here), copy-engine pushes
+after a local partition ("copy") and NCCL send/recv ("nccl") -- on two calls
+in a row with different inputs.
 """
 from __future__ import annotations
 
@@ -55,6 +57,8 @@ def _worker(rank, world, port, case, exchange, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["CUSORT_MGPU_EXCHANGE"] = exchange
+    if exchange == "pipe":
+        os.environ["CUSORT_MGPU_CHUNKS"] = "3"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     s = None
@@ -98,7 +102,7 @@ def _worker(rank, world, port, case, exchange, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
-@pytest.mark.parametrize("exchange", ["routed", "copy", "nccl"])
+@pytest.mark.parametrize("exchange", ["pipe", "routed", "copy", "nccl"])
 @pytest.mark.parametrize("case", [
     ("uniform", "u32", 1 << 20, 0, 32, False, True),
     ("uniform", "f32", 777_777, 0, 32, True, True),
