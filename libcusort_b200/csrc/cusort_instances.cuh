@@ -152,6 +152,10 @@ inline void fill_segmented(SegKernels* k) {
   k->small_warp.threads = 256;
   k->small_warp.tile = SegSmallLayout<KB, VB, FK, 1, KPT>::CAP;
   k->small_warp.smem = SegSmallLayout<KB, VB, FK, 1, KPT>::SMEM;
+  k->tiny.func = reinterpret_cast<const void*>(&seg_tiny_kernel<KB, VB, FK>);
+  k->tiny.threads = 256;
+  k->tiny.tile = 32;
+  k->tiny.smem = 0;
   k->small_block.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 8, KPT>);
   k->small_block.threads = 256;
   k->small_block.tile = SegSmallLayout<KB, VB, FK, 8, KPT>::CAP;

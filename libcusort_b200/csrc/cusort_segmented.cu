@@ -191,8 +191,9 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
     return launch(get_seg_copy_kernel((int)vb), seg_grid, 256, 0, false, &c, stream);
   }
 
-  // 1. small segments: one warp per segment up to the warp capacity, one CTA
-  //    per segment up to the block capacity
+  // 1. small segments: one warp per segment up to 32 items (all-pairs rank)
+  //    and up to the warp capacity (passes in shared memory), one CTA per
+  //    segment up to the block capacity
   SegSmallArgs sa = {};
   sa.keys_in = kin;
   sa.keys_out = kout;
@@ -207,9 +208,16 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
   sa.passes = P;
   sa.last_mask = last_mask;
   {
-    cudaError_t e = occupancy_of(k.small_warp, &sms, &occ);
+    cudaError_t e = occupancy_of(k.tiny, &sms, &occ);
     if (e) return e;
     sa.min_len = 1;
+    sa.max_len = (uint64_t)k.tiny.tile;
+    e = launch(k.tiny.func, (int)std::min<int64_t>((num_segments + 7) / 8, (int64_t)sms * occ), 256, 0, false, &sa,
+               stream);
+    if (e) return e;
+    e = occupancy_of(k.small_warp, &sms, &occ);
+    if (e) return e;
+    sa.min_len = (uint64_t)k.tiny.tile + 1;
     sa.max_len = (uint64_t)k.small_warp.tile;
     const int64_t want = (num_segments + 7) / 8;
     e = launch(k.small_warp.func, (int)std::min<int64_t>(want, (int64_t)sms * occ), 256, k.small_warp.smem, false,

@@ -5,6 +5,8 @@
 // DeviceSegmentedRadixSort (begin/end offset arrays in device memory).
 //
 // Segments are handled by length class, with no host synchronisation:
+//   * up to 32 items: one warp per segment, one item per lane, stable rank of
+//     the whole masked key by all-pairs comparison (seg_tiny_kernel);
 //   * up to 32*KPT items: one warp per segment, every pass in shared memory
 //     (seg_small_kernel<..., WPS = 1>);
 //   * up to 256*KPT items: one 256-thread CTA per segment, same scheme
@@ -258,6 +260,53 @@ __global__ void __launch_bounds__(256) seg_scan_kernel(const SegHistArgs a) {
     for (uint32_t w = 0; w < warp; ++w) pre += s_part[w];
     h[tid] = pre + incl - c;
     __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// tiny segments (at most 32 items): one warp per segment, one item per lane,
+// every pass at once: an item's output position is the number of items whose
+// masked key (all bits of [begin_bit, end_bit), twiddled) is smaller, or equal
+// and earlier in the segment -- a stable rank by all-pairs comparison over
+// warp shuffles, then one store per item.
+// ---------------------------------------------------------------------------
+template <int KB, int VB, bool FK>
+__global__ void __launch_bounds__(256) seg_tiny_kernel(const SegSmallArgs a) {
+  using K = typename dev::UIntOf<KB>::T;
+  using V = typename dev::UIntOf<(VB ? VB : 1)>::T;
+  constexpr bool HAS_V = VB > 0;
+  const uint32_t lane = threadIdx.x & 31u;
+  const K* keys_in = static_cast<const K*>(a.keys_in);
+  K* keys_out = static_cast<K*>(a.keys_out);
+  const V* vals_in = static_cast<const V*>(a.vals_in);
+  V* vals_out = static_cast<V*>(a.vals_out);
+  const K tc = (K)a.tw_c, tf = (K)a.tw_f;
+  const uint32_t nbits = 8u * (a.passes - 1u) + (uint32_t)__popc(a.last_mask);
+  const unsigned long long range = nbits >= 64 ? ~0ull : ((1ull << nbits) - 1ull);
+  const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
+  for (uint64_t s = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < a.num_segments; s += warps) {
+    const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
+    const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
+    if (len < a.min_len || len > a.max_len || len == 0) continue;  // uniform within the warp
+    const uint32_t n = (uint32_t)len;
+    const bool in = lane < n;
+    K k = K(0);
+    V v{};
+    if (in) {
+      k = keys_in[b + lane];
+      if constexpr (HAS_V) v = vals_in[b + lane];
+    }
+    const unsigned long long mk =
+        ((unsigned long long)dev::twiddle_k<FK, K>(k, tc, tf) >> a.begin_bit) & range;
+    uint32_t rank = 0;
+    for (uint32_t j = 0; j < n; ++j) {
+      const unsigned long long o = __shfl_sync(0xffffffffu, mk, j);
+      rank += (o < mk || (o == mk && j < lane)) ? 1u : 0u;
+    }
+    if (in) {
+      keys_out[b + rank] = k;
+      if constexpr (HAS_V) vals_out[b + rank] = v;
+    }
   }
 }
 

@@ -138,3 +138,16 @@ def test_segmented_many_tiny_segments():
     vals = np.arange(m, dtype=np.uint32)
     ko, vo, ek, ev = run_segmented("u16", keys, vals, b, e)
     assert same_bits(ko, ek) and same_bits(vo, ev)
+
+
+@pytest.mark.parametrize("kt", ["f64", "i8", "u32"])
+def test_segmented_class_boundaries(kt):
+    # lengths at the edges of the tiny (32), warp and CTA classes, with many ties
+    lengths = [31, 32, 33, 511, 512, 513, 4095, 4096, 4097, 2, 1, 0] * 3
+    b, e, n = lengths_segments(lengths, gap=2)
+    rng = np.random.default_rng(11)
+    keys = D.uniform_bits(kt, 64, seed=12)[rng.integers(0, 64, size=n)]
+    vals = np.arange(n, dtype=np.uint32)
+    for desc in (False, True):
+        ko, vo, ek, ev = run_segmented(kt, keys, vals, b, e, 0, 8 * keys.dtype.itemsize, desc)
+        assert same_bits(ko, ek) and same_bits(vo, ev)
