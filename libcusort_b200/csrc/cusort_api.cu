@@ -122,6 +122,8 @@ static void twiddle_constants(int kt, int kb, bool desc, uint64_t* c, uint64_t* 
 //   [digit histogram: passes x 256 x OffsetT]
 //   [lookback descriptors: tiles x 256 x OffsetT]     <- zeroed by init
 //   [staging keys n x K][staging values n x V]        <- in/out form, passes >= 2
+// (2-byte keys-only full-range sorts: control + counts[65536] + group
+// totals[256], all zeroed; nothing else)
 // ---------------------------------------------------------------------------
 struct Plan {
   int kt = 0, kb = 0, vb = 0, offb = 4;
@@ -134,6 +136,10 @@ struct Plan {
   uint64_t tiles = 0;
   size_t off_hist = 0, off_desc = 0, off_stage_k = 0, off_stage_v = 0, zero_bytes = 0, total = 0;
   bool staging = false;
+  // 2-byte keys-only over all 16 bits: one 16-bit digit (count, fill); the
+  // histogram region then holds counts[65536] and group totals[256]
+  bool fill16 = false;
+  KernelInfo h16, f16;
 };
 
 constexpr size_t kCtrlBytes = 256;
@@ -163,6 +169,19 @@ static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int e
     default: ok = false;
   }
   if (!ok) return false;
+  if (p->kb == 2 && p->vb == 0 && begin == 0 && end == 16) {
+    p->fill16 = get_fill16_kernels(p->offb, &p->h16, &p->f16);
+    if (p->fill16) {
+      p->tiles = 0;
+      p->off_hist = kCtrlBytes;
+      p->zero_bytes = kCtrlBytes + align256((size_t)(65536 + 256) * p->offb);
+      p->off_desc = p->zero_bytes;
+      p->staging = false;
+      p->off_stage_k = p->off_stage_v = p->off_desc;
+      p->total = p->off_desc;
+      return true;
+    }
+  }
   p->tiles = (n + p->os.tile - 1) / p->os.tile;
   p->off_hist = kCtrlBytes;
   p->off_desc = p->off_hist + align256((size_t)p->passes * kRadix * p->offb);
@@ -238,6 +257,7 @@ struct Launch {
     HistArgs hist;
     OnesweepArgs os;
     FillArgs fill;
+    Fill16Args f16;
   } args;
 };
 
@@ -275,6 +295,38 @@ static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers
     l.args.init.ptr = d_temp;
     l.args.init.n16 = n16;
     out->push_back(l);
+  }
+  if (p.fill16) {
+    // one 16-bit digit: count (CTA pairs split the bins), then fill the
+    // final destination (the last pass's output of the 8-bit schedule)
+    Fill16Args f;
+    f.keys = b.k_src[0];
+    f.counts = g_hist;
+    f.groups = g_hist + (size_t)65536 * p.offb;
+    f.out = b.k_dst[p.passes - 1];
+    f.n = p.n;
+    f.xor_c = (uint32_t)p.tw_c;
+    f.pad = 0;
+    int occ16 = 0;
+    CUSORT_TRY(get_occupancy(dev, p.h16, &occ16));
+    Launch l{};
+    l.func = p.h16.func;
+    l.grid = 2 * (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ16 / 2, p.n / 16384 + 1));
+    l.threads = p.h16.threads;
+    l.smem = p.h16.smem;
+    l.pdl = true;
+    l.kind = 1;
+    l.args.f16 = f;
+    out->push_back(l);
+    Launch l3{};
+    l3.func = p.f16.func;
+    l3.grid = 256 * 4;
+    l3.threads = p.f16.threads;
+    l3.pdl = true;
+    l3.kind = 2;
+    l3.args.f16 = f;
+    out->push_back(l3);
+    return cudaSuccess;
   }
   {
     Launch l{};

@@ -39,6 +39,9 @@ const void* get_seg_copy_kernel(int bytes);
 const void* get_init_kernel();
 // Count-and-fill kernel of 1-byte keys-only full-range sorts (kernels_k1.cu).
 const void* get_fill_bytes_kernel(int off_bytes);
+// 16-bit-digit count and fill kernels of 2-byte keys-only full-range sorts
+// (kernels_k2.cu).
+bool get_fill16_kernels(int off_bytes, KernelInfo* hist, KernelInfo* fill);
 
 // DoubleBuffer sort with `scratch` as its temp storage (cusort_api.cu).
 cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type, size_t value_bytes, bool descending,

@@ -179,6 +179,153 @@ __global__ void __launch_bounds__(256) fill_bytes_kernel(const FillArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// 16-bit digits for 16-bit keys-only sorts over all 16 bits (a one-pass
+// schedule: equal digits are equal keys, so counting is sorting).
+//   hist16_kernel: 1024-thread CTAs with 32768 shared u32 counters each; CTA
+//     pairs split the bins (blockIdx.x & 1 = top bit of the twiddled key) and
+//     the pairs split the keys (16-byte loads); at the end one global atomic
+//     per nonzero bin and one per group of 256 bins;
+//   fill16_kernel: each CTA owns one group of 256 consecutive bins (a
+//     contiguous output range, a quarter of it per CTA): its start is the sum
+//     of the lower groups' totals, the bins' starts a 256-wide scan; it writes
+//     every position's key, 8 keys (16 bytes) per store inside a run, warps on
+//     contiguous shares.
+// ---------------------------------------------------------------------------
+constexpr int kBins16 = 65536;
+
+template <typename Off>
+__global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
+  extern __shared__ __align__(16) uint32_t s_cnt16[];  // [32768]
+  dev::pdl_launch_dependents();
+  const uint32_t tid = threadIdx.x;
+  const uint32_t half = blockIdx.x & 1u;
+  const uint32_t part = blockIdx.x >> 1, parts = gridDim.x >> 1;
+  for (uint32_t i = tid; i < kBins16 / 2; i += 1024) s_cnt16[i] = 0;
+  __syncthreads();
+  const uint16_t* keys = static_cast<const uint16_t*>(a.keys);
+  const uint32_t xc = a.xor_c & 0xffffu;
+  auto count = [&](uint32_t k) {
+    const uint32_t t = (k ^ xc) & 0xffffu;
+    if ((t >> 15) == half) atomicAdd(s_cnt16 + (t & 0x7fffu), 1u);
+  };
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(keys);
+  uint64_t head = ((16 - (addr & 15)) & 15) / 2;
+  if (head > a.n) head = a.n;
+  const uint64_t nvec = (a.n - head) / 8;
+  const uint4* vec = reinterpret_cast<const uint4*>(keys + head);
+  const uint64_t stride = (uint64_t)parts * 1024;
+  for (uint64_t v = (uint64_t)part * 1024 + tid; v < nvec; v += stride) {
+    const uint4 x = dev::ld_stream_v4(vec + v);
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      count(w[e] & 0xffffu);
+      count(w[e] >> 16);
+    }
+  }
+  if (part == 0) {
+    for (uint64_t i = tid; i < head; i += 1024) count(keys[i]);
+    for (uint64_t i = head + nvec * 8 + tid; i < a.n; i += 1024) count(keys[i]);
+  }
+  __syncthreads();
+  dev::pdl_wait();  // counts zeroed by the init kernel
+  // coalesced flush (a warp's 32 bins share one line); each warp's 32 bins lie
+  // in one group of 256, whose total is gathered in shared memory first
+  __shared__ uint32_t s_grp[128];
+  if (tid < 128) s_grp[tid] = 0;
+  __syncthreads();
+  Off* g = static_cast<Off*>(a.counts) + (size_t)half * (kBins16 / 2);
+  const uint32_t lane = tid & 31u;
+  for (uint32_t i = tid; i < kBins16 / 2; i += 1024) {
+    const uint32_t c = s_cnt16[i];
+    if (c) atomicAdd(g + i, (Off)c);
+    uint32_t w = c;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (lane == 0 && w) atomicAdd(s_grp + (i >> 8), w);
+  }
+  __syncthreads();
+  if (tid < 128 && s_grp[tid]) atomicAdd(static_cast<Off*>(a.groups) + half * 128 + tid, (Off)s_grp[tid]);
+}
+
+template <typename Off>
+__global__ void __launch_bounds__(256) fill16_kernel(const Fill16Args a) {
+  __shared__ Off s_start[kRadix + 1];
+  __shared__ Off s_part[8];
+  dev::pdl_wait();  // counts from hist16_kernel
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t group = blockIdx.x >> 2, quarter = blockIdx.x & 3u;  // 256 groups of 256 bins
+  {
+    // group start = lower groups' totals; bin starts = exclusive scan of the counts
+    const Off gt = tid < group ? static_cast<const Off*>(a.groups)[tid] : Off(0);
+    const Off c = static_cast<const Off*>(a.counts)[(size_t)group * kRadix + tid];
+    Off gsum = gt;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, o);
+    Off incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const Off t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= (uint32_t)o) incl += t;
+    }
+    if (lane == 0) s_start[warp] = gsum;  // temporary: warp sums of the group totals
+    if (lane == 31) s_part[warp] = incl;
+    __syncthreads();
+    Off base = 0, pre = 0;
+    for (uint32_t w = 0; w < 8; ++w) base += s_start[w];
+    for (uint32_t w = 0; w < warp; ++w) pre += s_part[w];
+    __syncthreads();
+    s_start[tid] = base + pre + incl - c;
+    if (tid == kRadix - 1) s_start[kRadix] = base + pre + incl;
+    __syncthreads();
+  }
+  const uint64_t lo = s_start[0], hi = s_start[kRadix];
+  const uint64_t span = hi - lo, q0 = lo + span * quarter / 4, q1 = lo + span * (quarter + 1) / 4;
+  uint16_t* out = static_cast<uint16_t*>(a.out);
+  const uint32_t xc = a.xor_c & 0xffffu;
+  auto digit_at = [&](uint64_t i) {  // largest local bin b with start[b] <= i
+    uint32_t b = 0;
+#pragma unroll
+    for (uint32_t step = 128; step; step >>= 1)
+      if ((uint64_t)s_start[b + step] <= i) b += step;
+    return b;
+  };
+  auto key_of = [&](uint32_t b) { return (uint16_t)(((group << 8) | b) ^ xc); };
+  // unaligned head and ragged tail element by element
+  const uint64_t mis = (reinterpret_cast<uintptr_t>(out + q0) & 15) / 2;
+  uint64_t h = mis ? 8 - mis : 0;
+  if (h > q1 - q0) h = q1 - q0;
+  const uint64_t nvec = (q1 - q0 - h) / 8;
+  for (uint64_t i = q0 + tid; i < q0 + h; i += 256) out[i] = key_of(digit_at(i));
+  for (uint64_t i = q0 + h + nvec * 8 + tid; i < q1; i += 256) out[i] = key_of(digit_at(i));
+  // 8-key (16-byte) stores: each warp a contiguous share of the vectors, the
+  // lanes on consecutive vectors; a lane's bin only moves forward, so it is
+  // found once by binary search and then advanced
+  const uint64_t per = (nvec + 7) / 8, v0 = per * warp, v1 = v0 + per < nvec ? v0 + per : nvec;
+  const uint64_t p0 = q0 + h;
+  uint32_t b = 0;
+  bool found = false;
+  for (uint64_t v = v0 + lane; v < v1; v += 32) {
+    const uint64_t p = p0 + v * 8;
+    if (!found) {
+      b = digit_at(p);
+      found = true;
+    }
+    while ((uint64_t)s_start[b + 1] <= p) ++b;
+    if ((uint64_t)s_start[b + 1] >= p + 8) {
+      const uint32_t k2 = (uint32_t)key_of(b) * 0x10001u;
+      *reinterpret_cast<uint4*>(out + p) = make_uint4(k2, k2, k2, k2);
+    } else {
+      uint32_t bb = b;
+      for (int e = 0; e < 8; ++e) {
+        while ((uint64_t)s_start[bb + 1] <= p + e) ++bb;
+        out[p + e] = key_of(bb);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // onesweep: one stable LSD pass over digit (shift, mask).
 //
 // Persistent CTAs take tiles from a global ticket counter (so the lookback

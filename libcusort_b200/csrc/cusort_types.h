@@ -61,6 +61,20 @@ struct FillArgs {
   uint32_t xor_c;      // key = digit ^ xor_c (1-byte keys have no float twiddle)
 };
 
+// 16-bit keys-only sorts over all 16 bits: one 16-bit digit (65536 bins).
+// hist16: counts of the twiddled keys and of each group of 256 bins; each CTA
+// counts one half of the bins (blockIdx.x & 1) over its share of the keys.
+// fill16: the output is every key value repeated by its count.
+struct Fill16Args {
+  const void* keys;    // hist16: n 2-byte keys
+  void* counts;        // OffsetT[65536], zeroed by the init kernel
+  void* groups;        // OffsetT[256]: items per group of 256 bins, zeroed
+  void* out;           // fill16: n 2-byte keys
+  uint64_t n;
+  uint32_t xor_c;      // twiddled key = key ^ xor_c (2-byte keys have no float twiddle)
+  uint32_t pad;
+};
+
 struct OnesweepArgs {
   const void* keys_in;
   void* keys_out;

@@ -233,3 +233,24 @@ def test_byte_keys_count_fill(kt, desc, n):
     check(kt, keys, None, desc=desc)
     check(kt, keys, None, desc=desc, api="db")
     check(kt, keys, None, desc=desc, offset_items=3)
+
+
+# --- 2-byte keys-only over all 16 bits: one 16-bit digit (count, scan, fill) -----
+@pytest.mark.parametrize("kt", ["u16", "i16"])
+@pytest.mark.parametrize("desc", [False, True])
+@pytest.mark.parametrize("n", [2, 9, 1000, 65_537, 1_000_003, (1 << 22) + 5])
+def test_short_keys_one_pass(kt, desc, n):
+    keys = D.uniform_bits(kt, n, seed=n + 1)
+    if n > 100:
+        keys[: n // 4] = keys[1]  # one heavy value
+        keys[n // 4: n // 3] = keys[2]
+    check(kt, keys, None, desc=desc)
+    check(kt, keys, None, desc=desc, api="db")
+    check(kt, keys, None, desc=desc, offset_items=3)
+
+
+def test_short_keys_one_pass_few_values():
+    n = 777_777
+    keys = np.random.default_rng(1).choice(np.array([0, 1, 65535, 32768, 32767], dtype=np.uint16), size=n)
+    check("u16", keys, None)
+    check("i16", keys.view(np.int16), None, desc=True)
