@@ -50,11 +50,24 @@ namespace cusort_b200 {
 #define CUSORT_OS_KPT_K8V8 10
 #endif
 
+// 1-2 byte keys with 1-2 byte values keep their values in shared memory
+// (OnesweepCfg::VSMEM), so the register budget allows keys-only sized tiles;
+// 2+2 stays below the two-CTAs-per-SM shared-memory limit at 28.
+#ifndef CUSORT_OS_KPT_SMALLV
+#define CUSORT_OS_KPT_SMALLV 32
+#endif
+#ifndef CUSORT_OS_KPT_K2V2
+#define CUSORT_OS_KPT_K2V2 28
+#endif
+
 template <int KB, int VB>
 struct TileShape {
   static constexpr int THREADS = CUSORT_OS_THREADS;
   static constexpr int BYTES = KB + VB;
-  static constexpr int KPT = (KB == 8 && VB == 16)  ? CUSORT_OS_KPT_K8V16
+  static constexpr bool SMALLV = CUSORT_VSMEM && KB <= 2 && VB > 0 && VB <= 2;
+  static constexpr int KPT = (SMALLV && KB == 2 && VB == 2) ? CUSORT_OS_KPT_K2V2
+                             : SMALLV                       ? CUSORT_OS_KPT_SMALLV
+                             : (KB == 8 && VB == 16)  ? CUSORT_OS_KPT_K8V16
                              : (KB == 8 && VB == 8) ? CUSORT_OS_KPT_K8V8
                              : (VB == 0 && KB <= 4) ? CUSORT_OS_KPT_KEYS4
                              : (BYTES > 16)         ? CUSORT_OS_KPT_GT16

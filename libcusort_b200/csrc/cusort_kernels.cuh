@@ -630,6 +630,13 @@ struct OnesweepCfg {
   // 4-byte keys with 4-byte values move through shared memory as one 8-byte
   // item (one 64-bit store when scattering, one 64-bit load when writing out).
   static constexpr bool PACKED_KV = (KB_ == 4 && VB_ == 4);
+  // 1- and 2-byte keys with 1- or 2-byte values: the values stay in shared
+  // memory (copied from the staged tile straight to their sorted position in
+  // a second buffer), which frees KPT registers for larger tiles.
+#ifndef CUSORT_VSMEM
+#define CUSORT_VSMEM 1
+#endif
+  static constexpr bool VSMEM = CUSORT_VSMEM && VB_ > 0 && VB_ <= 2 && KB_ <= 2;
   // Mode 4 needs a key's digit twice (count, rank); recomputing it from the
   // key instead of keeping a digit array frees KPT registers, which buys
   // larger tiles (2 = every width, 1 = keys-only, 0 = never).
@@ -649,7 +656,9 @@ struct OnesweepCfg {
   // tile's digit prefix of earlier tiles' counts pre[256] + 8 warp totals
   // (u64); each owner's first and last digit [2][kMaxRouteRanks] (u32); per
   // digit the tile's destination addresses dk/dv[256] (u64)
-  static constexpr size_t OFF_ROUTE = OFF_MBAR + 2 * 8;
+  static constexpr size_t OFF_VOUT = align_up(OFF_MBAR + 2 * 8, 16);  // VSMEM: sorted values
+  static constexpr size_t VOUT_BYTES = VSMEM ? align_up((size_t)TILE * VB, 16) : 0;
+  static constexpr size_t OFF_ROUTE = OFF_VOUT + VOUT_BYTES;
   static constexpr size_t OFF_RPTR = OFF_ROUTE + kRadix;
   static constexpr size_t OFF_RPRE = OFF_RPTR + 4 * 8 * kMaxRouteRanks;
   static constexpr size_t OFF_RFIRST = OFF_RPRE + 8 * (kRadix + 8);
@@ -890,6 +899,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     const bool publish = (int64_t)tile != a.skip_tile;
     K* s_keys = reinterpret_cast<K*>(smem + (size_t)b * CFG::BUF_BYTES);
     V* s_vals = reinterpret_cast<V*>(smem + (size_t)b * CFG::BUF_BYTES + CFG::KEYS_BYTES);
+    // values in sorted tile order (the staged buffer itself unless VSMEM)
+    V* s_vsort = CFG::VSMEM ? reinterpret_cast<V*>(smem + CFG::OFF_VOUT) : s_vals;
+    constexpr bool VREG = HAS_V && !CFG::VSMEM;  // values held in registers
 
     // ---- 1. the tile's keys/values in shared memory
     bool use_tma = tma_tile(tile);
@@ -931,7 +943,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       const uint32_t idx = wfirst_c + s * 32 + lane;
       return (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
     };
-    V val[HAS_V ? KPT : 1];
+    V val[VREG ? KPT : 1];
     const uint32_t wfirst = wfirst_c;
     if constexpr (CFG::DIRECT_LOAD) {
       const K* kin = keys_in + base + wfirst + lane;
@@ -940,14 +952,14 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 #pragma unroll
         for (int s = 0; s < KPT; ++s) {
           key[s] = dev::ld_cs(kin + s * 32);
-          if constexpr (HAS_V) val[s] = dev::ld_cs(vin + s * 32);
+          if constexpr (VREG) val[s] = dev::ld_cs(vin + s * 32);
         }
       } else {
 #pragma unroll
         for (int s = 0; s < KPT; ++s) {
           const bool in = wfirst + s * 32 + lane < valid;
           key[s] = in ? dev::ld_cs(kin + s * 32) : K(0);
-          if constexpr (HAS_V) {
+          if constexpr (VREG) {
             if (in) val[s] = dev::ld_cs(vin + s * 32);
           }
         }
@@ -962,7 +974,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         const uint32_t idx = wfirst + s * 32 + lane;
         key[s] = s_keys[idx];
         if constexpr (!RECOMP) dr[s] = digit_at(s);
-        if constexpr (HAS_V) val[s] = s_vals[idx];
+        if constexpr (VREG) val[s] = s_vals[idx];
       }
     }
     uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
@@ -1019,7 +1031,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
             s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
           } else {
             s_keys[pos] = key[S];
-            if constexpr (HAS_V) s_vals[pos] = val[S];
+            if constexpr (VREG) s_vals[pos] = val[S];
+            if constexpr (CFG::VSMEM) s_vsort[pos] = s_vals[wfirst_c + S * 32 + lane];
           }
         });
       } else {
@@ -1030,7 +1043,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
             s_kv[pos] = make_uint2((uint32_t)key[s], (uint32_t)val[s]);
           } else {
             s_keys[pos] = key[s];
-            if constexpr (HAS_V) s_vals[pos] = val[s];
+            if constexpr (VREG) s_vals[pos] = val[s];
+            if constexpr (CFG::VSMEM) s_vsort[pos] = s_vals[wfirst_c + s * 32 + lane];
           }
         }
       }
@@ -1108,7 +1122,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
           v = (V)kv.y;
         } else {
           k = s_keys[j];
-          if constexpr (HAS_V) v = s_vals[j];
+          if constexpr (HAS_V) v = s_vsort[j];
         }
         const unsigned long long* s_dst = reinterpret_cast<const unsigned long long*>(smem + CFG::OFF_RDST);
         const uint32_t d = dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
@@ -1127,7 +1141,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         const K k = s_keys[j];
         const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
         keys_out[dst] = k;
-        if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+        if constexpr (HAS_V) vals_out[dst] = s_vsort[j];
       }
     };
     if (valid == (uint32_t)TILE) {
