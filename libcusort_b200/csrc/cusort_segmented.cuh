@@ -36,7 +36,7 @@ struct SegSmallShape {
 // ---------------------------------------------------------------------------
 // small segments: WPS warps sort one segment of at most WPS*32*KPT items, all
 // passes in shared memory, then one coalesced write.  Per pass: each warp
-// ranks its slots in order with __match_any_sync (rank among equal digits =
+// ranks its slots in order with a ballot match (rank among equal digits =
 // earlier slots' count + lower lanes of this slot), the group turns the
 // per-warp digit counts into offsets (digit-major, warp-minor: stable), and
 // every item is stored at its offset (in place: all items are in registers).
@@ -54,7 +54,7 @@ struct SegSmallLayout {
 };
 
 template <int KB, int VB, bool FK, int WPS, int KPT>
-__global__ void __launch_bounds__(256) seg_small_kernel(const SegSmallArgs a) {
+__global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a) {
   using K = typename dev::UIntOf<KB>::T;
   using V = typename dev::UIntOf<(VB ? VB : 1)>::T;
   using L = SegSmallLayout<KB, VB, FK, WPS, KPT>;
@@ -112,7 +112,9 @@ __global__ void __launch_bounds__(256) seg_small_kernel(const SegSmallArgs a) {
         key[sl] = in ? sk[i] : K(0);
         if constexpr (HAS_V) val[sl] = in ? sv[i] : V{};
         const uint32_t d = in ? dev::digit_k<FK, K>(key[sl], tc, tf, shift, mask) : 0x100u;
-        const uint32_t peers = __match_any_sync(0xffffffffu, d);
+        // peers: 8 ballots (about twice the rate of match.any on B200),
+        // restricted to the lanes inside the segment
+        const uint32_t peers = dev::match_digit_ballot<8>(d) & __ballot_sync(0xffffffffu, in);
         uint32_t before = 0;
         if (in) before = wc[d];
         __syncwarp();
