@@ -157,7 +157,7 @@ inline void fill_segmented(SegKernels* k) {
   fill_onesweep<KB, VB, Off, FK, false, true>(&k->onesweep);
   k->hist.func = reinterpret_cast<const void*>(&seg_hist_kernel<KB, Off, FK>);
   k->hist.threads = 512;
-  k->hist.smem = (size_t)KB * kRadix * 4;  // at most KB passes
+  k->hist.smem = (size_t)KB * kRadix * kSegHistReplicas * 4;  // at most KB passes
   k->scan.func = reinterpret_cast<const void*>(&seg_scan_kernel<Off>);
   k->scan.threads = 256;
   constexpr int KPT = SegSmallShape<KB, VB>::KPT;

@@ -31,26 +31,42 @@ namespace cusort_b200 {
 __global__ void __launch_bounds__(256) seg_plan_kernel(const SegPlanArgs a) {
   dev::pdl_wait();  // control block zeroed by the init kernel
   dev::pdl_launch_dependents();
+  // one segment per thread; the tile -> slot entries of the warp's segments
+  // are then written by the whole warp (one long segment would otherwise be
+  // written by a single thread)
   const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
-  for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s < a.num_segments; s += gthreads) {
-    const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
-    const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
-    if (len <= a.min_len) continue;
-    const uint64_t nt = (len + a.tile - 1) / a.tile;
-    const uint32_t slot = atomicAdd(&a.ctl->num_slots, 1u);
-    const uint32_t first = atomicAdd(&a.ctl->num_tiles, (uint32_t)nt);
-    if (slot >= a.max_slots || (uint64_t)first + nt > a.max_tiles) {
-      atomicOr(a.status, kStatusSegOverflow);
-      atomicOr(&a.ctl->pad[0], 1u);
-      continue;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint64_t first_s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x - lane;
+  for (uint64_t s0 = first_s; s0 < a.num_segments; s0 += gthreads) {
+    const uint64_t s = s0 + lane;
+    uint32_t slot = 0, first = 0, nt = 0;
+    if (s < a.num_segments) {
+      const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
+      const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
+      if (len > a.min_len) {
+        const uint64_t ntl = (len + a.tile - 1) / a.tile;
+        slot = atomicAdd(&a.ctl->num_slots, 1u);
+        first = atomicAdd(&a.ctl->num_tiles, (uint32_t)ntl);
+        if (slot >= a.max_slots || (uint64_t)first + ntl > a.max_tiles) {
+          atomicOr(a.status, kStatusSegOverflow);
+          atomicOr(&a.ctl->pad[0], 1u);
+        } else {
+          SegRecord r;
+          r.begin = (uint64_t)b;
+          r.len = len;
+          r.tile_first = first;
+          r.pad = 0;
+          a.recs[slot] = r;
+          nt = (uint32_t)ntl;
+        }
+      }
     }
-    SegRecord r;
-    r.begin = (uint64_t)b;
-    r.len = len;
-    r.tile_first = first;
-    r.pad = 0;
-    a.recs[slot] = r;
-    for (uint64_t t = 0; t < nt; ++t) a.tile_slot[first + t] = slot;
+    for (uint32_t j = 0; j < 32; ++j) {
+      const uint32_t nt_j = __shfl_sync(0xffffffffu, nt, j);
+      const uint32_t first_j = __shfl_sync(0xffffffffu, first, j);
+      const uint32_t slot_j = __shfl_sync(0xffffffffu, slot, j);
+      for (uint32_t t = lane; t < nt_j; t += 32) a.tile_slot[first_j + t] = slot_j;
+    }
   }
 }
 
@@ -269,8 +285,8 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
     ha.last_mask = last_mask;
     e = occupancy_of(k.hist, &sms, &occ);
     if (e) return e;
-    e = launch(k.hist.func, (int)std::min<uint64_t>((uint64_t)sms * occ, L.max_tiles), 512, (size_t)P * kRadix * 4,
-               true, &ha, stream);
+    e = launch(k.hist.func, (int)std::min<uint64_t>((uint64_t)sms * occ, L.max_tiles), 512,
+               (size_t)P * kRadix * kSegHistReplicas * 4, true, &ha, stream);
     if (e) return e;
     e = launch(k.scan.func, (int)std::min<uint64_t>((uint64_t)sms * 8, L.max_slots * P), 256, 0, true, &ha, stream);
     if (e) return e;

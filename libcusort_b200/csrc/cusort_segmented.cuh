@@ -187,10 +187,16 @@ __global__ void __launch_bounds__(256) seg_plan_kernel(const SegPlanArgs a);
 // ---------------------------------------------------------------------------
 // per-segment digit counts of every pass, one tile at a time
 // ---------------------------------------------------------------------------
+// Replicas of the per-segment counters: lane l counts into replica l % R
+// ([pass][digit][replica]), so a warp's shared atomics rarely collide.
+constexpr int kSegHistReplicas = 8;
+
 template <int KB, typename Off, bool FK>
 __global__ void __launch_bounds__(512) seg_hist_kernel(const SegHistArgs a) {
   using K = typename dev::UIntOf<KB>::T;
-  extern __shared__ __align__(16) uint32_t s_cnt[];  // [passes][256]
+  constexpr int R = kSegHistReplicas;
+  constexpr int PER = 16 / KB;  // keys per 16-byte load
+  extern __shared__ __align__(16) uint32_t s_cnt[];  // [passes][256][R]
   dev::pdl_wait();
   dev::pdl_launch_dependents();
   const uint32_t tid = threadIdx.x;
@@ -199,19 +205,33 @@ __global__ void __launch_bounds__(512) seg_hist_kernel(const SegHistArgs a) {
   const K* keys = static_cast<const K*>(a.keys);
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
   Off* hist = static_cast<Off*>(a.seg_hist);
+  uint32_t* my = s_cnt + (tid % R);
+  auto count = [&](K k) {
+    const K tw = dev::twiddle_k<FK, K>(k, tc, tf);
+    for (uint32_t p = 0; p < P; ++p) {
+      const uint32_t m = (p + 1 == P) ? a.last_mask : 0xffu;
+      atomicAdd(my + (p * kRadix + ((uint32_t)(tw >> (a.begin_bit + 8 * p)) & m)) * R, 1u);
+    }
+  };
   // Each CTA counts a contiguous range of tiles and flushes its counts when
   // the segment changes (and at the end), so a long segment costs one flush
   // per CTA, not one per tile.
   const uint32_t per = (num_tiles + gridDim.x - 1) / gridDim.x;
   const uint32_t t0 = blockIdx.x * per, t1 = min(num_tiles, t0 + per);
-  for (uint32_t i = tid; i < P * kRadix; i += blockDim.x) s_cnt[i] = 0;
+  for (uint32_t i = tid; i < P * kRadix * R; i += blockDim.x) s_cnt[i] = 0;
   __syncthreads();
   uint32_t cur_slot = 0xffffffffu;
   auto flush = [&]() {
     Off* h = hist + (size_t)cur_slot * P * kRadix;
     for (uint32_t i = tid; i < P * kRadix; i += blockDim.x) {
-      if (s_cnt[i]) atomicAdd(h + i, (Off)s_cnt[i]);
-      s_cnt[i] = 0;
+      uint32_t c = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t x = i * R + ((r + i) % R);  // rotated: conflict-free
+        c += s_cnt[x];
+        s_cnt[x] = 0;
+      }
+      if (c) atomicAdd(h + i, (Off)c);
     }
     __syncthreads();
   };
@@ -225,13 +245,20 @@ __global__ void __launch_bounds__(512) seg_hist_kernel(const SegHistArgs a) {
     const uint64_t off = (uint64_t)(t - r.tile_first) * a.tile;
     const uint64_t base = r.begin + off;
     const uint32_t valid = (uint32_t)((r.len - off) < (uint64_t)a.tile ? (r.len - off) : (uint64_t)a.tile);
-    for (uint32_t j = tid; j < valid; j += blockDim.x) {
-      const K tw = dev::twiddle_k<FK, K>(keys[base + j], tc, tf);
-      for (uint32_t p = 0; p < P; ++p) {
-        const uint32_t m = (p + 1 == P) ? a.last_mask : 0xffu;
-        atomicAdd(s_cnt + p * kRadix + ((uint32_t)(tw >> (a.begin_bit + 8 * p)) & m), 1u);
-      }
+    // 16-byte loads between the unaligned head and the ragged tail
+    const K* kp = keys + base;
+    uint32_t head = (uint32_t)(((16 - (reinterpret_cast<uintptr_t>(kp) & 15)) & 15) / KB);
+    if (head > valid) head = valid;
+    const uint32_t nvec = (valid - head) / PER;
+    const uint4* vec = reinterpret_cast<const uint4*>(kp + head);
+    for (uint32_t v = tid; v < nvec; v += blockDim.x) {
+      const uint4 x = dev::ld_stream_v4(vec + v);
+      const K* kk = reinterpret_cast<const K*>(&x);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) count(kk[e]);
     }
+    for (uint32_t j = tid; j < head; j += blockDim.x) count(kp[j]);
+    for (uint32_t j = head + nvec * PER + tid; j < valid; j += blockDim.x) count(kp[j]);
     __syncthreads();
   }
   if (cur_slot != 0xffffffffu) flush();
