@@ -50,22 +50,33 @@ namespace cusort_b200 {
 #define CUSORT_OS_KPT_K8V8 10
 #endif
 
-// 1-2 byte keys with 1-2 byte values keep their values in shared memory
-// (OnesweepCfg::VSMEM), so the register budget allows keys-only sized tiles;
-// 2+2 stays below the two-CTAs-per-SM shared-memory limit at 28.
+// Keys of up to 4 bytes with 1-2 byte values keep their values in shared
+// memory (OnesweepCfg::VSMEM), so the register budget allows larger tiles,
+// as large as two CTAs per SM fit in shared memory: 32 items per thread for
+// 1-2 byte keys (2+2: 28), 28 for 4+1 and 22 for 4+2.  Measured on B200 at
+// 2^26: u8+u8 0.327 -> 0.296 ms, u16+u8 0.668 -> 0.599, u16+u16 0.688 ->
+// 0.646, u32+u8 1.384 -> 1.292, u32+u16 1.451 -> 1.415.
 #ifndef CUSORT_OS_KPT_SMALLV
 #define CUSORT_OS_KPT_SMALLV 32
 #endif
 #ifndef CUSORT_OS_KPT_K2V2
 #define CUSORT_OS_KPT_K2V2 28
 #endif
+#ifndef CUSORT_OS_KPT_K4V1
+#define CUSORT_OS_KPT_K4V1 28
+#endif
+#ifndef CUSORT_OS_KPT_K4V2
+#define CUSORT_OS_KPT_K4V2 22
+#endif
 
 template <int KB, int VB>
 struct TileShape {
   static constexpr int THREADS = CUSORT_OS_THREADS;
   static constexpr int BYTES = KB + VB;
-  static constexpr bool SMALLV = CUSORT_VSMEM && KB <= 2 && VB > 0 && VB <= 2;
-  static constexpr int KPT = (SMALLV && KB == 2 && VB == 2) ? CUSORT_OS_KPT_K2V2
+  static constexpr bool SMALLV = CUSORT_VSMEM && KB <= CUSORT_VSMEM_MAXKB && VB > 0 && VB <= 2;
+  static constexpr int KPT = (SMALLV && KB == 4 && VB == 2) ? CUSORT_OS_KPT_K4V2
+                             : (SMALLV && KB == 4)          ? CUSORT_OS_KPT_K4V1
+                             : (SMALLV && KB == 2 && VB == 2) ? CUSORT_OS_KPT_K2V2
                              : SMALLV                       ? CUSORT_OS_KPT_SMALLV
                              : (KB == 8 && VB == 16)  ? CUSORT_OS_KPT_K8V16
                              : (KB == 8 && VB == 8) ? CUSORT_OS_KPT_K8V8

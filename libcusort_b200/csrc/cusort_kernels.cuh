@@ -630,13 +630,16 @@ struct OnesweepCfg {
   // 4-byte keys with 4-byte values move through shared memory as one 8-byte
   // item (one 64-bit store when scattering, one 64-bit load when writing out).
   static constexpr bool PACKED_KV = (KB_ == 4 && VB_ == 4);
-  // 1- and 2-byte keys with 1- or 2-byte values: the values stay in shared
+  // Keys of up to 4 bytes with 1- or 2-byte values: the values stay in shared
   // memory (copied from the staged tile straight to their sorted position in
   // a second buffer), which frees KPT registers for larger tiles.
 #ifndef CUSORT_VSMEM
 #define CUSORT_VSMEM 1
 #endif
-  static constexpr bool VSMEM = CUSORT_VSMEM && VB_ > 0 && VB_ <= 2 && KB_ <= 2;
+#ifndef CUSORT_VSMEM_MAXKB
+#define CUSORT_VSMEM_MAXKB 4
+#endif
+  static constexpr bool VSMEM = CUSORT_VSMEM && VB_ > 0 && VB_ <= 2 && KB_ <= CUSORT_VSMEM_MAXKB;
   // Mode 4 needs a key's digit twice (count, rank); recomputing it from the
   // key instead of keeping a digit array frees KPT registers, which buys
   // larger tiles (2 = every width, 1 = keys-only, 0 = never).
