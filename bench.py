@@ -149,7 +149,8 @@ def traffic_from_profiles(workload: str):
 class Sorter:
     """One SortPairs/SortKeys call through a C ABI (ours or the reference's)."""
 
-    def __init__(self, impl, torch, kt_name, kid, kb, vb, n, keys_in, keys_out, vals_in, vals_out, stream):
+    def __init__(self, impl, torch, kt_name, kid, kb, vb, n, keys_in, keys_out, vals_in, vals_out, stream,
+                 descending=False, begin_bit=0, end_bit=None):
         self.torch = torch
         self.impl = impl
         self.n = n
@@ -157,22 +158,25 @@ class Sorter:
         kin, kout = C.c_void_p(keys_in.data_ptr()), C.c_void_p(keys_out.data_ptr())
         vin = C.c_void_p(vals_in.data_ptr()) if vb else None
         vout = C.c_void_p(vals_out.data_ptr()) if vb else None
+        bb, eb = begin_bit, (8 * kb if end_bit is None else end_bit)
         if impl == "ours":
             from libcusort_b200 import _capi
             lib = _capi.load()
             if vb:
-                self.call = lambda t, tb: lib.cusort_sort_pairs(t, C.byref(tb), kid, kin, kout, vb, vin, vout, n, 0,
-                                                               8 * kb, s)
+                fn = lib.cusort_sort_pairs_descending if descending else lib.cusort_sort_pairs
+                self.call = lambda t, tb: fn(t, C.byref(tb), kid, kin, kout, vb, vin, vout, n, bb, eb, s)
             else:
-                self.call = lambda t, tb: lib.cusort_sort_keys(t, C.byref(tb), kid, kin, kout, n, 0, 8 * kb, s)
+                fn = lib.cusort_sort_keys_descending if descending else lib.cusort_sort_keys
+                self.call = lambda t, tb: fn(t, C.byref(tb), kid, kin, kout, n, bb, eb, s)
             self.lib = lib
         else:
             from oracle import oracle as O
             rl = O._load_ref()
             fn = getattr(rl, f"ref_sort_k{kid}")
             ks, vs = C.c_int(0), C.c_int(0)
-            self.call = lambda t, tb: fn(vb, 0, 1, t, C.byref(tb), kin, kout, C.byref(ks), vin, vout, C.byref(vs),
-                                         n, 0, 8 * kb, s)
+            dflag = int(bool(descending))
+            self.call = lambda t, tb: fn(vb, dflag, 1, t, C.byref(tb), kin, kout, C.byref(ks), vin, vout,
+                                         C.byref(vs), n, bb, eb, s)
         tb = C.c_size_t(0)
         rc = self.call(None, tb)
         if rc != 0:
@@ -332,6 +336,7 @@ def run_single(args, torch, dist=None, rank=0, world=1):
                   "path": "pinned host -> H2D -> sort (C ABI) -> D2H -> pinned host"}
     if not args.no_secondary:
         out["secondary"] = secondary(args, torch, device)
+        out["secondary"]["other_configs_2^26"] = other_configs(args, torch, device)
     if args.impl == "ours" and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds, n)
     if args.impl == "reference":
@@ -369,6 +374,65 @@ def secondary(args, torch, device):
         lib.cusort_set_kernel_timing(0)
         res["u32_keys_only_2^26"]["onesweep_launch_ms"] = statistics.mean(v)
         res["u32_keys_only_2^26"]["onesweep_gbs"] = 2 * n * 4 / (statistics.mean(v) * 1e-3) / 1e9
+    return res
+
+
+def other_configs(args, torch, device):
+    """The other BASELINE.json single-GPU configs at 2^26, same impl and API (in/out pointers),
+    seeded synthetic data with the configs' shapes and distributions: configs[1]'s low-entropy
+    variant, configs[2]'s keys-only dtype sweep (ascending and descending), configs[3]'s double
+    keys + 16-byte values and 20-bit Zipf keys.  Time per sort (CUDA events, 3 warm-up + 10)."""
+    n = 1 << args.log2n
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    stream = torch.cuda.current_stream().cuda_stream
+    dummy = torch.empty(1, dtype=torch.uint8, device=device)
+    res = {}
+
+    def words(bits):
+        lo, hi = (-(2 ** (bits - 1)), 2 ** (bits - 1)) if bits < 64 else (-(2 ** 63), 2 ** 63 - 1)
+        return torch.randint(lo, hi, (n,), dtype=torch.int64, device=device, generator=g)
+
+    def normal_specials(dtype, sigma):
+        x = torch.randn(n, dtype=dtype, device=device, generator=g) * sigma
+        idx = torch.randperm(n, device=device, generator=g)[: 5 * (n // 1000)].view(5, -1)
+        for row, v in zip(idx, (-0.0, 0.0, float("inf"), float("-inf"), float("nan"))):
+            x[row] = v
+        return x
+
+    def run(name, kt, kid, kb, keys, vals=None, vb=0, desc=False, begin=0, end=None):
+        kin = keys.contiguous().view(torch.uint8)
+        kout = torch.empty_like(kin)
+        vin = vals.contiguous().view(torch.uint8) if vb else dummy
+        vout = torch.empty_like(vin) if vb else dummy
+        srt = Sorter(args.impl, torch, kt, kid, kb, vb, n, kin, kout, vin, vout, stream, desc, begin, end)
+        ms = time_steps(torch, srt, 10, 3) / 10
+        res[name] = {"ms_per_step": round(ms, 4), "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2)}
+        del srt, kin, kout
+
+    a, b, c = words(32), words(32), words(32)
+    run("configs[1]_low_entropy_i32_u32_pairs", "i32", 5, 4, (a & b & c).to(torch.int32),
+        torch.arange(n, dtype=torch.int32, device=device), 4)
+    del a, b, c
+    for kt, kid, kb in (("i8", 1, 1), ("i16", 3, 2), ("i32", 5, 4), ("i64", 7, 8)):
+        w = words(8 * kb)
+        keys = w.to({1: torch.int8, 2: torch.int16, 4: torch.int32, 8: torch.int64}[kb])
+        for desc in (False, True):
+            run(f"configs[2]_{kt}_keys_{'desc' if desc else 'asc'}", kt, kid, kb, keys, desc=desc)
+    for kt, kid, kb, dt in (("f32", 8, 4, torch.float32), ("f64", 9, 8, torch.float64)):
+        keys = normal_specials(dt, 1e3)
+        for desc in (False, True):
+            run(f"configs[2]_{kt}_keys_{'desc' if desc else 'asc'}", kt, kid, kb, keys, desc=desc)
+    keys = torch.randn(n, dtype=torch.float64, device=device, generator=g)
+    idx = torch.arange(n, dtype=torch.int64, device=device)
+    vals = torch.stack([idx, ~idx], dim=1)  # ulonglong2 (index, ~index)
+    run("configs[3]_f64_keys_16B_values", "f64", 9, 8, keys, vals, 16)
+    del vals, idx
+    table = words(32).to(torch.int32)[:65536]
+    ranks = torch.arange(1, 65537, dtype=torch.float64, device=device)
+    draws = torch.multinomial((ranks ** -1.1).float(), n, replacement=True, generator=g)
+    run("configs[3]_u32_keys_bits_0_20_zipf_u32_values", "u32", 4, 4, table[draws],
+        torch.arange(n, dtype=torch.int32, device=device), 4, begin=0, end=20)
     return res
 
 
