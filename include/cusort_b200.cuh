@@ -163,6 +163,62 @@ struct DeviceRadixSort {
   }
 };
 
+// Segmented sort (no counterpart in the reference beyond the name in its
+// banner, libcusort.cuh:4): every segment [d_begin_offsets[s],
+// d_end_offsets[s]) sorted independently and stably into the same positions
+// of the output, CUB DeviceSegmentedRadixSort's argument order; offsets are
+// int64 arrays in device memory.  Forwards to cusort_segmented_sort_keys /
+// cusort_segmented_sort_pairs.
+struct DeviceSegmentedRadixSort {
+  template <typename KeyT, typename NumItemsT, typename NumSegmentsT>
+  static cudaError_t SortKeys(void* d_temp_storage, size_t& temp_storage_bytes, const KeyT* d_keys_in,
+                              KeyT* d_keys_out, NumItemsT num_items, NumSegmentsT num_segments,
+                              const int64_t* d_begin_offsets, const int64_t* d_end_offsets, int begin_bit = 0,
+                              int end_bit = sizeof(KeyT) * 8, cudaStream_t stream = 0) {
+    return cusort_segmented_sort_keys(d_temp_storage, &temp_storage_bytes, b200_detail::key_type_of<KeyT>(),
+                                      d_keys_in, d_keys_out, b200_detail::items(num_items),
+                                      b200_detail::items(num_segments), d_begin_offsets, d_end_offsets, begin_bit,
+                                      end_bit, 0, stream);
+  }
+
+  template <typename KeyT, typename NumItemsT, typename NumSegmentsT>
+  static cudaError_t SortKeysDescending(void* d_temp_storage, size_t& temp_storage_bytes, const KeyT* d_keys_in,
+                                        KeyT* d_keys_out, NumItemsT num_items, NumSegmentsT num_segments,
+                                        const int64_t* d_begin_offsets, const int64_t* d_end_offsets,
+                                        int begin_bit = 0, int end_bit = sizeof(KeyT) * 8, cudaStream_t stream = 0) {
+    return cusort_segmented_sort_keys(d_temp_storage, &temp_storage_bytes, b200_detail::key_type_of<KeyT>(),
+                                      d_keys_in, d_keys_out, b200_detail::items(num_items),
+                                      b200_detail::items(num_segments), d_begin_offsets, d_end_offsets, begin_bit,
+                                      end_bit, 1, stream);
+  }
+
+  template <typename KeyT, typename ValueT, typename NumItemsT, typename NumSegmentsT>
+  static cudaError_t SortPairs(void* d_temp_storage, size_t& temp_storage_bytes, const KeyT* d_keys_in,
+                               KeyT* d_keys_out, const ValueT* d_values_in, ValueT* d_values_out,
+                               NumItemsT num_items, NumSegmentsT num_segments, const int64_t* d_begin_offsets,
+                               const int64_t* d_end_offsets, int begin_bit = 0, int end_bit = sizeof(KeyT) * 8,
+                               cudaStream_t stream = 0) {
+    return cusort_segmented_sort_pairs(d_temp_storage, &temp_storage_bytes, b200_detail::key_type_of<KeyT>(),
+                                       d_keys_in, d_keys_out, b200_detail::value_bytes_of<ValueT>(), d_values_in,
+                                       d_values_out, b200_detail::items(num_items),
+                                       b200_detail::items(num_segments), d_begin_offsets, d_end_offsets, begin_bit,
+                                       end_bit, 0, stream);
+  }
+
+  template <typename KeyT, typename ValueT, typename NumItemsT, typename NumSegmentsT>
+  static cudaError_t SortPairsDescending(void* d_temp_storage, size_t& temp_storage_bytes, const KeyT* d_keys_in,
+                                         KeyT* d_keys_out, const ValueT* d_values_in, ValueT* d_values_out,
+                                         NumItemsT num_items, NumSegmentsT num_segments,
+                                         const int64_t* d_begin_offsets, const int64_t* d_end_offsets,
+                                         int begin_bit = 0, int end_bit = sizeof(KeyT) * 8, cudaStream_t stream = 0) {
+    return cusort_segmented_sort_pairs(d_temp_storage, &temp_storage_bytes, b200_detail::key_type_of<KeyT>(),
+                                       d_keys_in, d_keys_out, b200_detail::value_bytes_of<ValueT>(), d_values_in,
+                                       d_values_out, b200_detail::items(num_items),
+                                       b200_detail::items(num_segments), d_begin_offsets, d_end_offsets, begin_bit,
+                                       end_bit, 1, stream);
+  }
+};
+
 }  // namespace cusort
 
 #endif  // CUSORT_B200_CUH

@@ -146,16 +146,18 @@ def test_unaligned_pointers(kt, offset):
     check(kt, keys, D.values_for(n, 2), offset_items=offset, api="db")
 
 
-def test_graph_mode_matches_direct():
+@pytest.mark.parametrize("kt,vb", [("f32", 4), ("u16", 0), ("u8", 0), ("i16", 2)])
+def test_graph_mode_matches_direct(kt, vb):
+    # graph replay of every launch sequence: onesweep passes, 16-bit count + fill, 8-bit count + fill
     n = 1 << 18
     for seed in range(3):
-        keys = D.uniform_bits("f32", n, seed=seed)
-        vals = D.values_for(n, 4)
-        a = run_ours("f32", keys, vals, launch_mode=1)
-        b = run_ours("f32", keys, vals, launch_mode=0)
-        assert same_bits(a[0], b[0]) and same_bits(a[1], b[1])
-        ek, ev = O.oracle_sort("f32", keys, vals)
-        assert same_bits(a[0], ek) and same_bits(a[1], ev)
+        keys = D.uniform_bits(kt, n, seed=seed)
+        vals = D.values_for(n, vb) if vb else None
+        a = run_ours(kt, keys, vals, launch_mode=1)
+        b = run_ours(kt, keys, vals, launch_mode=0)
+        assert same_bits(a[0], b[0]) and (vals is None or same_bits(a[1], b[1]))
+        ek, ev = O.oracle_sort(kt, keys, vals)
+        assert same_bits(a[0], ek) and (vals is None or same_bits(a[1], ev))
 
 
 def test_torch_radix_sort():
