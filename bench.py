@@ -57,7 +57,7 @@ def parse():
                     help="N>1: global item count 2^this, split over the GPUs (strong scaling; default 32, configs[4])")
     ap.add_argument("--weak", action="store_true",
                     help="N>1: 2^log2n items per GPU (weak scaling) instead of the fixed global size")
-    ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs"], default=None,
+    ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs", "i32_u32_pairs_lowent"], default=None,
                     help="only run --warmup + --steps sorts of this case (for ncu captures)")
     return ap.parse_args()
 
@@ -445,6 +445,10 @@ def profile_case(args, torch):
     else:
         kt, kid, kb, vb = "i32", 5, 4, 4
     keys, vals = make_inputs(torch, n, seed=2, device=device)
+    if args.profile_case == "i32_u32_pairs_lowent":  # configs[1]'s low-entropy keys: a & b & c
+        b, c = make_inputs(torch, n, seed=3, device=device)[0], make_inputs(torch, n, seed=4, device=device)[0]
+        keys = keys & b & c
+        del b, c
     kin, vin = keys.view(torch.uint8), vals.view(torch.uint8)
     kout, vout = torch.empty_like(kin), torch.empty_like(vin)
     s = Sorter(args.impl, torch, kt, kid, kb, vb, n, kin, kout, vin, vout, torch.cuda.current_stream().cuda_stream)
