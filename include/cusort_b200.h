@@ -142,7 +142,9 @@ cudaError_t cusort_sort_pairs_wide(void* d_temp_storage, size_t* temp_storage_by
  * memory.  It calls no cudaMalloc, cudaFree or allocating library routine.
  *   - Limit: a call whose temp storage would exceed the array returns
  *     cudaErrorInvalidValue and does nothing.  The temp storage is about
- *     1 KiB per 8192-item tile plus 2 KiB (e.g. 2^25 32-bit keys fit in 4 MiB).
+ *     1 KiB per tile (2 KiB from 2^30 items on) plus a few KiB, a tile being
+ *     4096 to 18432 items by key and value width (e.g. 2^26 32-bit keys, or
+ *     2^25 32-bit keys with 32-bit values, fit in 4 MiB).
  *   - The array occupies CUSORT_NOALLOC_SCRATCH_BYTES on every GPU where this
  *     entry point has run, until the process exits.
  *   - The first call on each device looks up the array's device address

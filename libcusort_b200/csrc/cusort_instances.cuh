@@ -24,10 +24,11 @@ namespace cusort_b200 {
 // Items per thread (KPT) by bytes per item; overridable for tuning.  Larger
 // tiles amortise the per-tile work (column scan, block scan, lookback,
 // ticket) over more keys; the limit is 64 registers per thread at two 512-
-// thread CTAs per SM.  Measured on B200 at 2^26 items: u32 keys-only 32
-// (pass 0.302 -> 0.251 ms vs 16), int32/uint32 pairs 20 (0.369 -> 0.356 ms).
+// thread CTAs per SM.  Measured on B200 at 2^26 items: u32 keys-only 36
+// (pass 0.302 -> 0.251 ms from 16 to 32; whole sort 1.045 -> 1.026 ms from 32
+// to 36, 40 and 44 slower), int32/uint32 pairs 20 (0.369 -> 0.356 ms vs 16).
 #ifndef CUSORT_OS_KPT_KEYS4
-#define CUSORT_OS_KPT_KEYS4 32
+#define CUSORT_OS_KPT_KEYS4 36
 #endif
 #ifndef CUSORT_OS_KPT_LE8
 #define CUSORT_OS_KPT_LE8 20

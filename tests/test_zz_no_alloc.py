@@ -82,7 +82,12 @@ def test_no_alloc_keys_only_matches():
 
 
 def test_no_alloc_rejects_sizes_beyond_the_scratch():
-    n = 1 << 26  # needs ~8 MiB of temp storage, more than the fixed scratch
+    n = 1 << 27  # needs ~7 MiB of temp storage, more than the fixed scratch
+    lib = _capi.load()
+    need = C.c_size_t(0)
+    db = _capi.DoubleBufferC()
+    assert lib.cusort_sort_keys_db(None, C.byref(need), _capi.KEY_TYPES["u32"], C.byref(db), n, 0, 32, None) == 0
+    assert need.value > SCRATCH_BYTES
     keys = np.zeros(n, dtype=np.uint32)
     rc, *_ = sort_noalloc("u32", keys)
     assert rc == _capi.CUDA_ERROR_INVALID_VALUE
