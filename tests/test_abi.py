@@ -117,3 +117,19 @@ def test_settings_roundtrip():
     assert lib.cusort_set_wait_limit_ns(prev) == 123
     assert lib.cusort_debug_set_skip_tile(5) == -1
     assert lib.cusort_debug_set_skip_tile(-1) == 5
+
+
+def test_short_keys_one_digit_temp():
+    # 2-byte keys-only over all 16 bits use one 16-bit digit: counts[65536] + group totals[256]
+    # after the 256-byte control block, no descriptors and no staging (either API form)
+    n = 1 << 26
+    for kt in (2, 3):  # u16, i16
+        for raw in (True, False):
+            rc, nb = _query_keys(kt, n, 0, 16, raw=raw)
+            assert rc == 0 and nb == 256 + (65536 + 256) * 4
+    # a partial range sorts by 8-bit onesweep passes again (in/out form: staging)
+    rc, nb = _query_keys(2, n, 0, 15, raw=True)
+    assert rc == 0 and nb > n * 2
+    # with values, too
+    rc, nb = _query_pairs(2, 2, n, 0, 16)
+    assert rc == 0 and nb > n * 4
