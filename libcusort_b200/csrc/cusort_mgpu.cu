@@ -235,6 +235,15 @@ struct MgpuLayout {
 
 // Temp storage of one call; the local sorts' sizes come from this library's
 // own size queries.
+// CUSORT_MGPU_FORCE_EXCHANGE=1: a 1-rank communicator runs the whole
+// pipeline (counts, all-gather, partition + exchange to itself, fence, local
+// sort) instead of a plain sort -- a test hook for the exchange kernels on
+// one GPU.
+bool force_exchange() {
+  const char* v = std::getenv("CUSORT_MGPU_FORCE_EXCHANGE");
+  return v && v[0] == '1';
+}
+
 cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, int begin, int end, bool desc,
                    MgpuLayout* L) {
   const int kb = key_bytes(kt);
@@ -242,7 +251,7 @@ cudaError_t layout(int kt, size_t vb, int64_t n_local, int64_t cap, int nranks, 
   size_t part_tmp = 0, final_tmp = 0, single_tmp = 0;
   cusort_double_buffer kd = {}, vd = {};
   cudaError_t e;
-  if (nranks == 1) {  // a plain single-GPU sort in the temp storage
+  if (nranks == 1 && !force_exchange()) {  // a plain single-GPU sort in the temp storage
     e = vb ? cusort_sort_pairs(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, vb, nullptr, nullptr,
                                n_local, begin, end, nullptr)
            : cusort_sort_keys(nullptr, &single_tmp, (cusort_key_type)kt, nullptr, nullptr, n_local, begin, end,
@@ -428,7 +437,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   void* stmp = t + L.sort_tmp;
   size_t stmp_bytes = L.sort_tmp_bytes;
 
-  if (nranks == 1) {
+  if (nranks == 1 && !force_exchange()) {
     if (n_local > out_capacity) return cudaErrorInvalidValue;
     if (vb)
       e = desc ? cusort_sort_pairs_descending(stmp, &stmp_bytes, key_type, d_keys_in, d_keys_out, vb, d_values_in,

@@ -42,6 +42,34 @@ def test_single_rank_communicator_matches_oracle():
         s.close()
 
 
+@pytest.mark.parametrize("exchange", ["routed", "pipe", "copy", "nccl"])
+@pytest.mark.parametrize("kt,vdtype", [("u32", np.uint16), ("i16", np.uint8), ("f32", None), ("f64", np.uint64),
+                                       ("u8", np.uint16)])
+def test_single_rank_full_exchange_pipeline(monkeypatch, exchange, kt, vdtype):
+    # The exchange kernels (routed partition into the receive buffer, chunked routing, copy-engine
+    # and NCCL exchanges) on one GPU: a 1-rank communicator forced through the whole pipeline.
+    monkeypatch.setenv("CUSORT_MGPU_FORCE_EXCHANGE", "1")
+    monkeypatch.setenv("CUSORT_MGPU_EXCHANGE", exchange)
+    monkeypatch.setenv("CUSORT_MGPU_CHUNKS", "3")
+    s = mgpu.ShardedSorter(0, 1, mgpu.ShardedSorter.unique_id())
+    try:
+        n = 400_003
+        for seed in (5, 6):  # two calls into the same buffers
+            keys = D.zipf_table(kt, n, seed=seed, distinct=4096)
+            vals = None if vdtype is None else np.random.default_rng(seed).integers(
+                0, np.iinfo(vdtype).max, size=n, dtype=vdtype)
+            kd = torch.from_numpy(np.ascontiguousarray(keys)).cuda()
+            vd = None if vals is None else torch.from_numpy(vals.view(
+                {1: np.int8, 2: np.int16, 8: np.int64}[vals.dtype.itemsize])).cuda()
+            ko, vo = s.sort(kd, vd, capacity=n)
+            ek, ev = O.oracle_sort(kt, keys, vals)
+            assert np.array_equal(ko.cpu().numpy().view(np.uint8), ek.view(np.uint8))
+            if vals is not None:
+                assert np.array_equal(vo.cpu().numpy().view(vals.dtype), ev)
+    finally:
+        s.close()
+
+
 def _port():
     so = socket.socket()
     so.bind(("127.0.0.1", 0))
