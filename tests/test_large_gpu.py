@@ -78,3 +78,30 @@ def test_64bit_offsets_above_2p30(api):
     seen = torch.zeros(n, dtype=torch.bool, device="cuda")
     seen[vo.to(torch.int64)] = True
     assert bool(seen.all())
+
+
+@pytest.mark.skipif(torch.cuda.is_available() and _free_gb() < 40, reason="needs ~25 GB of device memory")
+@pytest.mark.parametrize("kt,np_dtype,bits", [("u16", torch.int16, 16), ("u8", torch.uint8, 8)])
+def test_count_fill_paths_above_2p30(kt, np_dtype, bits):
+    # 1- and 2-byte keys-only full-range sorts (count and fill, one digit) with 64-bit counts:
+    # the output is sorted and holds every key value exactly as often as the input
+    lib = _capi.load()
+    n = (1 << 30) + 777
+    g = torch.Generator(device="cuda")
+    g.manual_seed(31)
+    keys = torch.randint(0, 1 << bits, (n,), dtype=torch.int32, device="cuda", generator=g).to(np_dtype)
+    keys[: n // 5] = 3  # a heavy value
+    kout = torch.empty_like(keys)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    nb = C.c_size_t(0)
+    kid = _capi.KEY_TYPES[kt]
+    assert lib.cusort_sort_keys(None, C.byref(nb), kid, P(keys), P(kout), n, 0, bits, stream) == 0
+    temp = torch.empty(nb.value, dtype=torch.uint8, device="cuda")
+    assert lib.cusort_sort_keys(P(temp), C.byref(nb), kid, P(keys), P(kout), n, 0, bits, stream) == 0
+    torch.cuda.synchronize()
+    mask = (1 << bits) - 1
+    ki = keys.to(torch.int64) & mask  # unsigned key value
+    ko = kout.to(torch.int64) & mask
+    assert bool((ko[1:] >= ko[:-1]).all()), "keys not sorted"
+    assert torch.equal(torch.bincount(ki, minlength=1 << bits), torch.bincount(ko, minlength=1 << bits))
