@@ -19,7 +19,12 @@ one complete sort call (init + histogram + 4 onesweep passes).
 --impl reference times the UNMODIFIED reference library compiled for sm_100a
 (oracle/_ref) on the same workload through its own public API.
 
-N>1 (torchrun): sharded multi-GPU sort, 2^26 pairs per GPU (weak scaling).
+secondary  u32 keys-only 2^26; the other BASELINE.json single-GPU configs at
+            2^26; configs[0] (2^20 u32 keys-only, 4 MiB: L2-resident, so a
+            hot-L2, launch-latency-bound figure), direct and graph launches
+
+N>1 (torchrun): sharded multi-GPU sort of 2^32 int32/uint32 pairs split over
+the GPUs (strong scaling, configs[4]); --weak for 2^26 pairs per GPU.
 """
 from __future__ import annotations
 
@@ -248,9 +253,29 @@ def cpu_baseline(seconds: float, n_full: int):
         t_total += time.perf_counter() - t0
         reps += 1
     rate = reps * m / t_total / 1e9
+    # one-thread std::stable_sort of the same sample, bounded to about a fifth of the time
+    reps1, t1 = 0, 0.0
+    while t1 < seconds / 5 and reps1 < 100:
+        t0 = time.perf_counter()
+        O.oracle_sort("i32", keys, vals, 0, 32, False, threads=1)
+        t1 += time.perf_counter() - t0
+        reps1 += 1
     return {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{reps} x {m} int32/uint32 pairs (2^{m.bit_length() - 1}), __gnu_parallel::stable_sort "
-                      f"over {cores} OpenMP threads, {t_total:.1f} s"}
+                      f"over {cores} OpenMP threads, {t_total:.1f} s",
+            "cpu_model": cpu_model(),
+            "single_thread": {"value": reps1 * m / t1 / 1e9, "unit": UNIT, "cores": 1,
+                              "sample": f"{reps1} x {m} pairs, std::stable_sort, {t1:.1f} s"}}
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def run_single(args, torch, dist=None, rank=0, world=1):
@@ -337,6 +362,7 @@ def run_single(args, torch, dist=None, rank=0, world=1):
     if not args.no_secondary:
         out["secondary"] = secondary(args, torch, device)
         out["secondary"]["other_configs_2^26"] = other_configs(args, torch, device)
+        out["secondary"]["configs[0]_u32_keys_2^20_hot_l2"] = small_hot_l2(args, torch, device)
     if args.impl == "ours" and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds, n)
     if args.impl == "reference":
@@ -375,6 +401,41 @@ def secondary(args, torch, device):
         res["u32_keys_only_2^26"]["onesweep_launch_ms"] = statistics.mean(v)
         res["u32_keys_only_2^26"]["onesweep_gbs"] = 2 * n * 4 / (statistics.mean(v) * 1e-3) / 1e9
     return res
+
+
+def small_hot_l2(args, torch, device):
+    """2^20 u32 keys-only (seeded uniform), ascending, 4 passes.  The 4 MiB input
+    and output stay in the 126 MB L2 between steps, so this is a hot-L2, launch-latency-bound
+    figure (not an HBM one): back-to-back sorts, CUDA events around 200 of them.  Ours is timed
+    with direct launches and with the cached CUDA graph; the reference's default build (CUDA
+    12.9) has direct launches only."""
+    n = 1 << 20
+    steps = 200
+    try:
+        g = torch.Generator(device=device)
+        g.manual_seed(1)
+        kin = torch.randint(0, 256, (n * 4,), dtype=torch.uint8, device=device, generator=g)
+        kout = torch.empty_like(kin)
+        dummy = torch.empty(1, dtype=torch.uint8, device=device)
+        s = Sorter(args.impl, torch, "u32", 4, 4, 0, n, kin, kout, dummy, dummy,
+                   torch.cuda.current_stream().cuda_stream)
+        res = {"n": n, "l2": "hot (4 MiB input, no flush)", "bound": "launch latency"}
+        modes = [("direct", 0), ("graph", 1)] if args.impl == "ours" else [("direct", None)]
+        for name, mode in modes:
+            if mode is not None:
+                s.lib.cusort_set_launch_mode(mode)
+            ms = time_steps(torch, s, steps, 10) / steps
+            res[name] = {"us_per_sort": round(ms * 1e3, 2), "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2)}
+        if args.impl == "ours":
+            s.lib.cusort_set_launch_mode(0)
+        ko = kout.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        res["sorted"] = bool((ko[1:] >= ko[:-1]).all().item())
+        return res
+    except Exception as e:  # the headline line must not depend on this informational leg
+        if args.impl == "ours":
+            from libcusort_b200 import _capi
+            _capi.load().cusort_set_launch_mode(0)
+        return {"error": f"{type(e).__name__}: {e}"}
 
 
 def other_configs(args, torch, device):
