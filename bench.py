@@ -21,7 +21,8 @@ one complete sort call (init + histogram + 4 onesweep passes).
 
 secondary  u32 keys-only 2^26; the other BASELINE.json single-GPU configs at
             2^26; configs[0] (2^20 u32 keys-only, 4 MiB: L2-resident, so a
-            hot-L2, launch-latency-bound figure), direct and graph launches
+            hot-L2, launch-latency-bound figure), direct and graph launches;
+            ours only: segmented sort of 2^26 pairs, one entry per length class
 
 N>1 (torchrun): sharded multi-GPU sort of 2^32 int32/uint32 pairs split over
 the GPUs (strong scaling, configs[4]); --weak for 2^26 pairs per GPU.
@@ -62,7 +63,8 @@ def parse():
                     help="N>1: global item count 2^this, split over the GPUs (strong scaling; default 32, configs[4])")
     ap.add_argument("--weak", action="store_true",
                     help="N>1: 2^log2n items per GPU (weak scaling) instead of the fixed global size")
-    ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs", "i32_u32_pairs_lowent"], default=None,
+    ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs", "i32_u32_pairs_lowent", "u16_keys",
+                                               "seg_i32_u32_pairs_1000"], default=None,
                     help="only run --warmup + --steps sorts of this case (for ncu captures)")
     return ap.parse_args()
 
@@ -363,6 +365,8 @@ def run_single(args, torch, dist=None, rank=0, world=1):
         out["secondary"] = secondary(args, torch, device)
         out["secondary"]["other_configs_2^26"] = other_configs(args, torch, device)
         out["secondary"]["configs[0]_u32_keys_2^20_hot_l2"] = small_hot_l2(args, torch, device)
+        if args.impl == "ours":
+            out["secondary"]["segmented_2^26"] = segmented(args, torch, device)
     if args.impl == "ours" and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds, n)
     if args.impl == "reference":
@@ -438,6 +442,63 @@ def small_hot_l2(args, torch, device):
         return {"error": f"{type(e).__name__}: {e}"}
 
 
+def seg_call(torch, keys, vals, kout, vout, seglen, stream):
+    """Segmented SortPairs (int32 keys, uint32 values) over equal-length segments of `seglen`
+    items (the last one shorter) through cusort_segmented_sort_pairs; returns the sort callable."""
+    from libcusort_b200 import _capi
+    lib = _capi.load()
+    n = keys.numel()
+    S = (n + seglen - 1) // seglen
+    b = torch.arange(S, dtype=torch.int64, device=keys.device) * seglen
+    e = torch.clamp(b + seglen, max=n)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    nb = C.c_size_t(0)
+    s = C.c_void_p(stream)
+    args = lambda t: (t, C.byref(nb), 5, P(keys), P(kout), 4, P(vals), P(vout), n, S, P(b), P(e), 0, 32, 0, s)  # noqa: E731
+    if lib.cusort_segmented_sort_pairs(*args(None)) != 0:
+        raise RuntimeError("segmented size query failed")
+    temp = torch.empty(max(nb.value, 1), dtype=torch.uint8, device=keys.device)
+
+    def call():
+        if lib.cusort_segmented_sort_pairs(*args(P(temp))) != 0:
+            raise RuntimeError("segmented sort failed")
+    call.keep = (b, e, temp)
+    call.segments = S
+    return call
+
+
+def segmented(args, torch, device):
+    """Segmented sort (CUB DeviceSegmentedRadixSort semantics; the reference has none) of 2^26
+    int32 keys + uint32 index values in equal-length segments, one entry per length class: the
+    warp all-pairs class (16), the warp and CTA shared-memory classes (1000, 4000) and the
+    segmented onesweep (2^20).  3 warm-up + 10 timed sorts each; inputs > L2.  The first and
+    last segment of each timed output are checked against torch's stable sort."""
+    n = 1 << args.log2n
+    res = {}
+    try:
+        g = torch.Generator(device=device)
+        g.manual_seed(1)
+        keys = torch.randint(-(2 ** 31), 2 ** 31, (n,), dtype=torch.int64, device=device, generator=g).to(torch.int32)
+        vals = torch.arange(n, dtype=torch.int32, device=device)
+        kout, vout = torch.empty_like(keys), torch.empty_like(vals)
+        stream = torch.cuda.current_stream().cuda_stream
+        for seglen in (16, 1000, 4000, 1 << 20):
+            call = seg_call(torch, keys, vals, kout, vout, seglen, stream)
+            ms = time_steps(torch, call, 10, 3) / 10
+            ok = True
+            for i in (0, call.segments - 1):
+                a0, a1 = i * seglen, min(n, (i + 1) * seglen)
+                ref = torch.sort(keys[a0:a1], stable=True)
+                ok &= bool(torch.equal(ref.values, kout[a0:a1])) and bool(torch.equal(vals[a0:a1][ref.indices],
+                                                                                       vout[a0:a1]))
+            res[f"seglen_{seglen}"] = {"segments": call.segments, "ms_per_step": round(ms, 4),
+                                       "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2), "checked": ok}
+        return res
+    except Exception as e:  # informational leg: keep the headline line
+        res["error"] = f"{type(e).__name__}: {e}"
+        return res
+
+
 def other_configs(args, torch, device):
     """The other BASELINE.json single-GPU configs at 2^26, same impl and API (in/out pointers),
     seeded synthetic data with the configs' shapes and distributions: configs[1]'s low-entropy
@@ -501,6 +562,25 @@ def profile_case(args, torch):
     """Plain sorts of one case, nothing else (the command that ncu captures)."""
     device = torch.device("cuda", 0)
     n = 1 << args.log2n
+    if args.profile_case == "u16_keys":  # one 16-bit digit: hist16 + fill16
+        g = torch.Generator(device=device)
+        g.manual_seed(1)
+        kin = torch.randint(0, 256, (n * 2,), dtype=torch.uint8, device=device, generator=g)
+        kout = torch.empty_like(kin)
+        dummy = torch.empty(1, dtype=torch.uint8, device=device)
+        s = Sorter(args.impl, torch, "u16", 2, 2, 0, n, kin, kout, dummy, dummy,
+                   torch.cuda.current_stream().cuda_stream)
+    elif args.profile_case == "seg_i32_u32_pairs_1000":  # segmented, 1000-item segments (CTA class)
+        keys, vals = make_inputs(torch, n, seed=1, device=device)
+        kout, vout = torch.empty_like(keys), torch.empty_like(vals)
+        s = seg_call(torch, keys, vals, kout, vout, 1000, torch.cuda.current_stream().cuda_stream)
+    if args.profile_case in ("u16_keys", "seg_i32_u32_pairs_1000"):
+        for _ in range(args.warmup + args.steps):
+            s()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": args.profile_case, "n": n, "impl": args.impl,
+                          "sorts": args.warmup + args.steps}))
+        return
     if args.profile_case == "u32_keys":
         kt, kid, kb, vb = "u32", 4, 4, 0
     else:

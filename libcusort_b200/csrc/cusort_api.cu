@@ -182,6 +182,11 @@ static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int e
       return true;
     }
   }
+  // Fewer items: smaller tiles, so the persistent grid still covers the SMs.
+  if (n <= kMidTileMaxItems) {
+    KernelInfo small;
+    if (get_small_onesweep(p->kb, p->vb, fk, n <= kSmallTileMaxItems ? 0 : 1, &small)) p->os = small;
+  }
   p->tiles = (n + p->os.tile - 1) / p->os.tile;
   p->off_hist = kCtrlBytes;
   p->off_desc = p->off_hist + align256((size_t)p->passes * kRadix * p->offb);

@@ -8,6 +8,13 @@
 
 struct cusort_double_buffer;
 
+#ifndef CUSORT_SMALL_TILE_MAX_ITEMS
+#define CUSORT_SMALL_TILE_MAX_ITEMS (1ull << 20)
+#endif
+#ifndef CUSORT_MID_TILE_MAX_ITEMS
+#define CUSORT_MID_TILE_MAX_ITEMS (1ull << 23)
+#endif
+
 namespace cusort_b200 {
 
 struct KernelInfo {
@@ -23,6 +30,14 @@ bool get_kernels_k1(int value_bytes, int off_bytes, bool float_key, KernelInfo* 
 bool get_kernels_k2(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 bool get_kernels_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
 bool get_kernels_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep, KernelInfo* histogram);
+// Smaller-tile onesweep kernels (32-bit offsets) for sorts of at most
+// kSmallTileMaxItems (tier 0) or kMidTileMaxItems (tier 1) items; false where
+// the key/value widths have none (kernels_small.cu).
+constexpr uint64_t kSmallTileMaxItems = CUSORT_SMALL_TILE_MAX_ITEMS;
+constexpr uint64_t kMidTileMaxItems = CUSORT_MID_TILE_MAX_ITEMS;
+static_assert(kSmallTileMaxItems <= kMidTileMaxItems && kMidTileMaxItems < (1ull << 30),
+              "smaller-tile kernels use 32-bit offsets");
+bool get_small_onesweep(int key_bytes, int value_bytes, bool float_key, int tier, KernelInfo* onesweep);
 // Routed onesweep kernels (kernels_routed_*.cu): the multi-GPU partition pass.
 bool get_routed_k12(int key_bytes, int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);
 bool get_routed_k4(int value_bytes, int off_bytes, bool float_key, KernelInfo* onesweep);

@@ -70,6 +70,21 @@ namespace cusort_b200 {
 #define CUSORT_OS_KPT_K4V2 22
 #endif
 
+// Small sorts of 4-byte keys (keys-only or with 4-byte values): a 2^20-key
+// sort has only 57 tiles of 512 x 36 keys, so most of the 148 SMs would sit
+// idle in every pass.  Up to kSmallTileMaxItems items the tiles hold 8 items
+// per thread, up to kMidTileMaxItems 16.  Measured on B200 (u32 keys-only /
+// int32+uint32 pairs, us per sort, tile 36 or 20 -> 8 -> 16): 2^16 82 / 64 ->
+// 33 / 35 -> 39 / 43; 2^20 72 / 81 -> 53 / 59 -> 59 / 72; 2^21 99 / 88 -> 80
+// / 92 -> 66 / 78; 2^23 213 / 239 -> 233 / 268 -> 176 / 218; 2^24 309 / 417
+// -> 430 / 514 -> 328 / 422.
+#ifndef CUSORT_OS_KPT_SMALL_TILE
+#define CUSORT_OS_KPT_SMALL_TILE 8
+#endif
+#ifndef CUSORT_OS_KPT_MID_TILE
+#define CUSORT_OS_KPT_MID_TILE 16
+#endif
+
 template <int KB, int VB>
 struct TileShape {
   static constexpr int THREADS = CUSORT_OS_THREADS;
@@ -95,6 +110,15 @@ template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG =
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB>;
   using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>;
+  os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
+  os->threads = CFG::THREADS;
+  os->tile = CFG::TILE;
+  os->smem = CFG::SMEM_BYTES;
+}
+
+template <int KB, int VB, bool FK, int KPT>
+inline void fill_onesweep_small(KernelInfo* os) {
+  using CFG = OnesweepCfg<KB, VB, unsigned int, CUSORT_OS_THREADS, KPT, CUSORT_OS_MINB, FK>;
   os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;
   os->tile = CFG::TILE;

@@ -108,6 +108,33 @@ def test_offset_width_switch():
     assert p.value == 4
 
 
+def _tile_items(kt, vb, n):
+    lib = _capi.load()
+    t = C.c_int(0)
+    assert lib.cusort_query_plan(kt, vb, n, 0, 8 * _capi.KEY_BYTES[[k for k, v in _capi.KEY_TYPES.items()
+                                                                    if v == kt][0]],
+                                 None, C.byref(t), None, None, None) == 0
+    return t.value
+
+
+@pytest.mark.parametrize("kt", [4, 5, 8])  # u32, i32, f32
+@pytest.mark.parametrize("vb,big", [(0, 512 * 36), (4, 512 * 20)])
+def test_tile_tiers(kt, vb, big):
+    # 4-byte keys, keys-only or 4-byte values: 8 items per thread up to 2^20 items, 16 up to
+    # 2^23, the large tile above (so a small sort's grid still covers the SMs)
+    assert _tile_items(kt, vb, 2) == 512 * 8
+    assert _tile_items(kt, vb, 1 << 20) == 512 * 8
+    assert _tile_items(kt, vb, (1 << 20) + 1) == 512 * 16
+    assert _tile_items(kt, vb, 1 << 23) == 512 * 16
+    assert _tile_items(kt, vb, (1 << 23) + 1) == big
+    assert _tile_items(kt, vb, 1 << 26) == big
+
+
+def test_tile_tiers_other_widths_unchanged():
+    for kt, vb in ((4, 8), (4, 2), (6, 0), (2, 4)):
+        assert _tile_items(kt, vb, 1 << 16) == _tile_items(kt, vb, 1 << 26)
+
+
 def test_settings_roundtrip():
     lib = _capi.load()
     assert lib.cusort_set_launch_mode(1) == 0

@@ -90,6 +90,25 @@ def test_sizes(vb):
         check("u32", keys, vals)
 
 
+# --- the three tile sizes of 4-byte keys (8 / 16 / large items per thread by item count) --
+@pytest.mark.parametrize("tier_n", [1 << 20, 1 << 23, 1 << 26])
+@pytest.mark.parametrize("kt,vb,desc", [("u32", 0, False), ("i32", 4, False), ("f32", 4, True)])
+def test_tile_tiers(tier_n, kt, vb, desc):
+    # sizes at a multiple of the tier's tile -1 / 0 / +1, as close to the tier's upper end as
+    # the tier allows (the large tile just above 2^23, where it takes over)
+    t = tile_of(kt, vb, tier_n)
+    if tier_n > (1 << 23):
+        m = (1 << 23) // t + 1
+        sizes = [m * t - 1, m * t, m * t + 1]
+    else:
+        m = tier_n // t
+        sizes = [m * t - 1, m * t, (m - 1) * t + 1]
+    for n in sizes:
+        assert tile_of(kt, vb, n) == t
+        keys = D.uniform_bits(kt, n, seed=n % 1000)
+        check(kt, keys, D.values_for(n, vb) if vb else None, desc=desc)
+
+
 # --- distributions ------------------------------------------------------------
 @pytest.mark.parametrize("kt", ["f32", "f64"])
 @pytest.mark.parametrize("desc", [False, True])
