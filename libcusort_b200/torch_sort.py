@@ -32,13 +32,46 @@ def key_type_of(dtype: torch.dtype) -> str:
 
 
 def _value_bytes(values: torch.Tensor, n: int) -> int:
-    if values.shape[0] != n:
+    if values.dim() < 1 or values.shape[0] != n:
         raise ValueError("values must have the item count as leading dimension")
     if not values.is_contiguous():
         raise ValueError("values must be contiguous")
-    vb = values.numel() * values.element_size() // max(n, 1)
+    vb = values.element_size()
+    for d in values.shape[1:]:
+        vb *= d
     if vb not in (1, 2, 4, 8, 16):
         raise ValueError(f"value payload of {vb} bytes per item is not supported (1, 2, 4, 8 or 16)")
+    return vb
+
+
+def _check_like(name: str, t: torch.Tensor, ref: torch.Tensor) -> None:
+    """An output tensor must match its input in dtype, shape and device and be contiguous:
+    the kernels write exactly the input's bytes into it."""
+    if t.dtype != ref.dtype or t.shape != ref.shape or t.device != ref.device or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous tensor of the input's dtype, shape and device "
+                         f"(got {t.dtype}, {tuple(t.shape)}, {t.device})")
+
+
+def _check_args(keys, values, out_keys, out_values, temp) -> int:
+    """Shape, type and device checks of radix_sort's tensors; returns the value bytes per item
+    (0 for keys-only).  No CUDA call."""
+    if keys.dim() != 1 or not keys.is_contiguous():
+        raise ValueError("keys must be a contiguous 1-D tensor")
+    key_type_of(keys.dtype)
+    n = keys.numel()
+    vb = 0
+    if values is not None:
+        if values.device != keys.device:
+            raise ValueError(f"values are on {values.device}, keys on {keys.device}")
+        vb = _value_bytes(values, n)
+        if out_values is not None:
+            _check_like("out_values", out_values, values)
+    elif out_values is not None:
+        raise ValueError("out_values given without values")
+    if out_keys is not None:
+        _check_like("out_keys", out_keys, keys)
+    if temp is not None and (temp.device != keys.device or temp.dtype != torch.uint8 or not temp.is_contiguous()):
+        raise ValueError("temp must be a contiguous uint8 tensor on the keys' device")
     return vb
 
 
@@ -74,16 +107,13 @@ def radix_sort(keys: torch.Tensor, values: torch.Tensor | None = None, *, descen
     """Stable radix sort; returns (sorted_keys, sorted_values_or_None). Inputs are not modified."""
     if not keys.is_cuda:
         raise ValueError("keys must be a CUDA tensor (this path has no CPU implementation)")
-    if keys.dim() != 1 or not keys.is_contiguous():
-        raise ValueError("keys must be a contiguous 1-D tensor")
+    vb = _check_args(keys, values, out_keys, out_values, temp)
     lib = _capi.load()
     kt = key_type_of(keys.dtype)
     n = keys.numel()
     end_bit = 8 * keys.element_size() if end_bit is None else end_bit
     out_keys = torch.empty_like(keys) if out_keys is None else out_keys
-    vb = 0
-    if values is not None:
-        vb = _value_bytes(values, n)
+    if vb:
         out_values = torch.empty_like(values) if out_values is None else out_values
     need = temp_storage_bytes(kt, n, vb, begin_bit, end_bit, raw=True)
     if temp is None or temp.numel() < need:

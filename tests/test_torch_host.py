@@ -1,0 +1,76 @@
+"""Host-side argument checks of the PyTorch wrapper (no GPU: meta and CPU tensors).
+
+Every output, value and temp tensor is checked against the keys before any CUDA call, since the
+kernels write exactly the input's bytes into the outputs."""
+from __future__ import annotations
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from libcusort_b200.torch_sort import _check_args, radix_sort  # noqa: E402
+
+M = "meta"
+
+
+def _k(n=10, dtype=torch.int32):
+    return torch.empty(n, dtype=dtype, device=M)
+
+
+def test_cpu_tensor_is_rejected():
+    with pytest.raises(ValueError, match="CUDA"):
+        radix_sort(torch.arange(10, dtype=torch.int32))
+
+
+def test_value_widths():
+    k = _k(10)
+    assert _check_args(k, None, None, None, None) == 0
+    assert _check_args(k, torch.empty(10, dtype=torch.int8, device=M), None, None, None) == 1
+    assert _check_args(k, torch.empty(10, 2, dtype=torch.int64, device=M), None, None, None) == 16
+    assert _check_args(k, torch.empty(10, 2, dtype=torch.int16, device=M), None, None, None) == 4
+    with pytest.raises(ValueError, match="3 bytes"):
+        _check_args(k, torch.empty(10, 3, dtype=torch.uint8, device=M), None, None, None)
+    with pytest.raises(ValueError, match="leading dimension"):
+        _check_args(k, torch.empty(11, dtype=torch.int32, device=M), None, None, None)
+
+
+def test_empty_inputs_keep_their_value_width():
+    k = _k(0)
+    assert _check_args(k, torch.empty(0, 2, dtype=torch.int64, device=M), None, None, None) == 16
+    assert _check_args(k, torch.empty(0, dtype=torch.int32, device=M), None, None, None) == 4
+
+
+def test_outputs_must_match_inputs():
+    k = _k(10)
+    v = torch.empty(10, dtype=torch.int64, device=M)
+    with pytest.raises(ValueError, match="out_keys"):
+        _check_args(k, None, _k(9), None, None)
+    with pytest.raises(ValueError, match="out_keys"):
+        _check_args(k, None, _k(10, torch.float32), None, None)
+    with pytest.raises(ValueError, match="out_keys"):
+        _check_args(k, None, torch.empty(20, dtype=torch.int32, device=M)[::2], None, None)
+    with pytest.raises(ValueError, match="out_values"):
+        _check_args(k, v, None, torch.empty(10, dtype=torch.int32, device=M), None)
+    with pytest.raises(ValueError, match="out_values given without values"):
+        _check_args(k, None, None, v, None)
+    assert _check_args(k, v, _k(10), torch.empty_like(v), None) == 8
+
+
+def test_devices_and_temp():
+    k = _k(10)
+    with pytest.raises(ValueError, match="values are on"):
+        _check_args(k, torch.empty(10, dtype=torch.int32), None, None, None)
+    with pytest.raises(ValueError, match="out_keys"):
+        _check_args(k, None, torch.empty(10, dtype=torch.int32), None, None)
+    with pytest.raises(ValueError, match="temp"):
+        _check_args(k, None, None, None, torch.empty(100, dtype=torch.int32, device=M))
+    with pytest.raises(ValueError, match="temp"):
+        _check_args(k, None, None, None, torch.empty(100, dtype=torch.uint8))
+    assert _check_args(k, None, None, None, torch.empty(100, dtype=torch.uint8, device=M)) == 0
+
+
+def test_key_shape_and_dtype():
+    with pytest.raises(ValueError, match="1-D"):
+        _check_args(torch.empty(2, 5, dtype=torch.int32, device=M), None, None, None, None)
+    with pytest.raises(TypeError, match="unsupported key dtype"):
+        _check_args(torch.empty(5, dtype=torch.bool, device=M), None, None, None, None)

@@ -60,3 +60,17 @@ def test_ops_under_torch_compile():
     x = torch.randn(65_537, device="cuda")
     cf = torch.compile(f, backend="aot_eager", fullgraph=True)
     assert torch.equal(cf(x), f(x))
+
+
+@pytest.mark.gpu
+@gpu
+@pytest.mark.parametrize("n", [0, 1, 2])
+def test_ops_tiny_and_empty(n):
+    # trivial sizes with a 16-byte payload per item (the payload width comes from the shape,
+    # not from numel / n)
+    x = torch.arange(n, 0, -1, device="cuda", dtype=torch.int32)
+    v = torch.stack([torch.arange(n, device="cuda"), -torch.arange(n, device="cuda")], dim=1)
+    sk, sv = torch.ops.cusort.sort_pairs(x, v)
+    ref = torch.sort(x, stable=True)
+    assert torch.equal(sk, ref.values) and torch.equal(sv, v[ref.indices])
+    assert torch.equal(torch.ops.cusort.argsort(x), ref.indices)
