@@ -11,7 +11,15 @@ import ctypes as C
 import torch
 
 from . import _capi
-from .torch_sort import key_type_of
+from .torch_sort import _check_args, key_type_of
+
+
+def _check_output(name: str, t: torch.Tensor, ref: torch.Tensor, cap: int) -> None:
+    """Other ranks write up to `cap` items into an output through IPC: it must hold them."""
+    if (t.dtype != ref.dtype or t.device != ref.device or not t.is_contiguous() or t.dim() != ref.dim()
+            or t.shape[1:] != ref.shape[1:] or t.shape[0] < cap):
+        raise ValueError(f"{name} must be a contiguous tensor of the input's dtype, device and row shape with at "
+                         f"least capacity={cap} rows (got {t.dtype}, {tuple(t.shape)}, {t.device})")
 
 
 class ShardedSorter:
@@ -53,17 +61,25 @@ class ShardedSorter:
              begin_bit: int = 0, end_bit: int | None = None, descending: bool = False, out_keys=None,
              out_values=None):
         """Sorts this rank's slice as part of the global sort; returns this rank's (keys, values) part."""
+        if not keys.is_cuda:
+            raise ValueError("keys must be a CUDA tensor (this path has no CPU implementation)")
+        vb = _check_args(keys, values, None, None, None)
+        if out_values is not None and values is None:
+            raise ValueError("out_values given without values")
         kt = key_type_of(keys.dtype)
         n = keys.numel()
         end_bit = 8 * keys.element_size() if end_bit is None else end_bit
-        vb = 0
-        if values is not None:
-            vb = values.numel() * values.element_size() // max(n, 1)
         cap = capacity if capacity is not None else 2 * n + 4096
+        if cap < 0:
+            raise ValueError("capacity must be >= 0")
         if out_keys is None:
             out_keys = torch.empty(cap, dtype=keys.dtype, device=keys.device)
+        else:
+            _check_output("out_keys", out_keys, keys, cap)
         if vb and out_values is None:
             out_values = torch.empty((cap,) + tuple(values.shape[1:]), dtype=values.dtype, device=keys.device)
+        elif vb:
+            _check_output("out_values", out_values, values, cap)
         kin = C.c_void_p(keys.data_ptr())
         vin = C.c_void_p(values.data_ptr()) if vb else None
         kout = C.c_void_p(out_keys.data_ptr())

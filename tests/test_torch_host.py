@@ -74,3 +74,17 @@ def test_key_shape_and_dtype():
         _check_args(torch.empty(2, 5, dtype=torch.int32, device=M), None, None, None, None)
     with pytest.raises(TypeError, match="unsupported key dtype"):
         _check_args(torch.empty(5, dtype=torch.bool, device=M), None, None, None, None)
+
+
+def test_sharded_output_capacity():
+    from libcusort_b200.mgpu import _check_output
+    k = _k(10)
+    _check_output("out_keys", _k(64), k, 64)
+    with pytest.raises(ValueError, match="capacity=64"):
+        _check_output("out_keys", _k(63), k, 64)
+    with pytest.raises(ValueError, match="out_keys"):
+        _check_output("out_keys", _k(64, torch.int64), k, 64)
+    v = torch.empty(10, 2, dtype=torch.int64, device=M)
+    _check_output("out_values", torch.empty(64, 2, dtype=torch.int64, device=M), v, 64)
+    with pytest.raises(ValueError, match="out_values"):
+        _check_output("out_values", torch.empty(128, dtype=torch.int64, device=M), v, 64)
