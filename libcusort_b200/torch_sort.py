@@ -3,7 +3,11 @@
 ``radix_sort(keys, values=None, descending=False, begin_bit=0, end_bit=None)``
 is a stable LSD radix sort of a 1-D CUDA tensor (plus an optional payload
 tensor whose leading dimension is the item count) through
-``cusort_sort_keys`` / ``cusort_sort_pairs`` of include/cusort_b200.h.
+``cusort_sort_keys`` / ``cusort_sort_pairs`` of include/cusort_b200.h; payload
+rows of other widths than 1, 2, 4, 8 or 16 bytes go through
+``cusort_sort_pairs_wide``.  ``segmented_sort`` sorts every segment
+[begin_offsets[s], end_offsets[s]) independently through
+``cusort_segmented_sort_keys`` / ``cusort_segmented_sort_pairs``.
 Temporary storage is a uint8 CUDA tensor from torch's caching allocator; the
 work runs on torch's current stream.
 """
@@ -31,7 +35,10 @@ def key_type_of(dtype: torch.dtype) -> str:
         raise TypeError(f"unsupported key dtype {dtype}") from None
 
 
-def _value_bytes(values: torch.Tensor, n: int) -> int:
+_NATIVE_VB = (1, 2, 4, 8, 16)
+
+
+def _value_bytes(values: torch.Tensor, n: int, any_width: bool = False) -> int:
     if values.dim() < 1 or values.shape[0] != n:
         raise ValueError("values must have the item count as leading dimension")
     if not values.is_contiguous():
@@ -39,7 +46,7 @@ def _value_bytes(values: torch.Tensor, n: int) -> int:
     vb = values.element_size()
     for d in values.shape[1:]:
         vb *= d
-    if vb not in (1, 2, 4, 8, 16):
+    if vb < 1 or (not any_width and vb not in _NATIVE_VB):
         raise ValueError(f"value payload of {vb} bytes per item is not supported (1, 2, 4, 8 or 16)")
     return vb
 
@@ -52,7 +59,7 @@ def _check_like(name: str, t: torch.Tensor, ref: torch.Tensor) -> None:
                          f"(got {t.dtype}, {tuple(t.shape)}, {t.device})")
 
 
-def _check_args(keys, values, out_keys, out_values, temp) -> int:
+def _check_args(keys, values, out_keys, out_values, temp, any_width: bool = False) -> int:
     """Shape, type and device checks of radix_sort's tensors; returns the value bytes per item
     (0 for keys-only).  No CUDA call."""
     if keys.dim() != 1 or not keys.is_contiguous():
@@ -63,7 +70,7 @@ def _check_args(keys, values, out_keys, out_values, temp) -> int:
     if values is not None:
         if values.device != keys.device:
             raise ValueError(f"values are on {values.device}, keys on {keys.device}")
-        vb = _value_bytes(values, n)
+        vb = _value_bytes(values, n, any_width)
         if out_values is not None:
             _check_like("out_values", out_values, values)
     elif out_values is not None:
@@ -104,10 +111,12 @@ def temp_storage_bytes(key_type: str, n: int, value_bytes: int = 0, begin_bit: i
 def radix_sort(keys: torch.Tensor, values: torch.Tensor | None = None, *, descending: bool = False,
                begin_bit: int = 0, end_bit: int | None = None, out_keys: torch.Tensor | None = None,
                out_values: torch.Tensor | None = None, temp: torch.Tensor | None = None):
-    """Stable radix sort; returns (sorted_keys, sorted_values_or_None). Inputs are not modified."""
+    """Stable radix sort; returns (sorted_keys, sorted_values_or_None). Inputs are not modified.
+    Payload rows of any width are accepted (1, 2, 4, 8 and 16 bytes move with the keys; other
+    widths are gathered by the sorted permutation)."""
     if not keys.is_cuda:
         raise ValueError("keys must be a CUDA tensor (this path has no CPU implementation)")
-    vb = _check_args(keys, values, out_keys, out_values, temp)
+    vb = _check_args(keys, values, out_keys, out_values, temp, any_width=True)
     lib = _capi.load()
     kt = key_type_of(keys.dtype)
     n = keys.numel()
@@ -115,14 +124,26 @@ def radix_sort(keys: torch.Tensor, values: torch.Tensor | None = None, *, descen
     out_keys = torch.empty_like(keys) if out_keys is None else out_keys
     if vb:
         out_values = torch.empty_like(values) if out_values is None else out_values
-    need = temp_storage_bytes(kt, n, vb, begin_bit, end_bit, raw=True)
+    kid = _capi.key_type_id(kt)
+    wide = vb and vb not in _NATIVE_VB
+    if wide:
+        q = C.c_size_t(0)
+        _capi.check(lib.cusort_sort_pairs_wide(None, C.byref(q), kid, None, None, vb, None, None, n, begin_bit,
+                                               end_bit, int(descending), None), "size query")
+        need = q.value
+    else:
+        need = temp_storage_bytes(kt, n, vb, begin_bit, end_bit, raw=True)
     if temp is None or temp.numel() < need:
         temp = torch.empty(max(need, 1), dtype=torch.uint8, device=keys.device)
     nbytes = C.c_size_t(temp.numel())
     stream = C.c_void_p(torch.cuda.current_stream(keys.device).cuda_stream)
-    kid = _capi.key_type_id(kt)
     with torch.cuda.device(keys.device):
-        if vb:
+        if wide:
+            rc = lib.cusort_sort_pairs_wide(C.c_void_p(temp.data_ptr()), C.byref(nbytes), kid,
+                                            C.c_void_p(keys.data_ptr()), C.c_void_p(out_keys.data_ptr()), vb,
+                                            C.c_void_p(values.data_ptr()), C.c_void_p(out_values.data_ptr()), n,
+                                            begin_bit, end_bit, int(descending), stream)
+        elif vb:
             fn = lib.cusort_sort_pairs_descending if descending else lib.cusort_sort_pairs
             rc = fn(C.c_void_p(temp.data_ptr()), C.byref(nbytes), kid, C.c_void_p(keys.data_ptr()),
                     C.c_void_p(out_keys.data_ptr()), vb, C.c_void_p(values.data_ptr()),
@@ -132,6 +153,58 @@ def radix_sort(keys: torch.Tensor, values: torch.Tensor | None = None, *, descen
             rc = fn(C.c_void_p(temp.data_ptr()), C.byref(nbytes), kid, C.c_void_p(keys.data_ptr()),
                     C.c_void_p(out_keys.data_ptr()), n, begin_bit, end_bit, stream)
     _capi.check(rc, "cusort sort")
+    return out_keys, (out_values if vb else None)
+
+
+def _check_offsets(keys: torch.Tensor, begin_offsets: torch.Tensor, end_offsets: torch.Tensor) -> int:
+    """Segment offsets: int64, 1-D, contiguous, equal lengths, on the keys' device.  Returns the
+    segment count.  No CUDA call."""
+    for name, t in (("begin_offsets", begin_offsets), ("end_offsets", end_offsets)):
+        if t.dtype != torch.int64 or t.dim() != 1 or not t.is_contiguous() or t.device != keys.device:
+            raise ValueError(f"{name} must be a contiguous 1-D int64 tensor on the keys' device "
+                             f"(got {t.dtype}, {tuple(t.shape)}, {t.device})")
+    if begin_offsets.numel() != end_offsets.numel():
+        raise ValueError("begin_offsets and end_offsets must have the same length")
+    return begin_offsets.numel()
+
+
+def segmented_sort(keys: torch.Tensor, begin_offsets: torch.Tensor, end_offsets: torch.Tensor,
+                   values: torch.Tensor | None = None, *, descending: bool = False, begin_bit: int = 0,
+                   end_bit: int | None = None, out_keys: torch.Tensor | None = None,
+                   out_values: torch.Tensor | None = None):
+    """Sorts every segment [begin_offsets[s], end_offsets[s]) of keys (and values) stably and
+    independently into the same positions (CUB DeviceSegmentedRadixSort semantics; the segments
+    must not overlap).  Positions outside every segment are not written: fresh outputs start as
+    copies of the inputs, so they keep the input there.  Returns (keys, values_or_None)."""
+    if not keys.is_cuda:
+        raise ValueError("keys must be a CUDA tensor (this path has no CPU implementation)")
+    vb = _check_args(keys, values, out_keys, out_values, None)
+    S = _check_offsets(keys, begin_offsets, end_offsets)
+    lib = _capi.load()
+    kt = key_type_of(keys.dtype)
+    kid = _capi.key_type_id(kt)
+    n = keys.numel()
+    end_bit = 8 * keys.element_size() if end_bit is None else end_bit
+    out_keys = keys.clone() if out_keys is None else out_keys
+    if vb:
+        out_values = values.clone() if out_values is None else out_values
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    stream = C.c_void_p(torch.cuda.current_stream(keys.device).cuda_stream)
+    nbytes = C.c_size_t(0)
+
+    def call(tp):
+        if vb:
+            return lib.cusort_segmented_sort_pairs(tp, C.byref(nbytes), kid, P(keys), P(out_keys), vb, P(values),
+                                                   P(out_values), n, S, P(begin_offsets), P(end_offsets),
+                                                   begin_bit, end_bit, int(descending), stream)
+        return lib.cusort_segmented_sort_keys(tp, C.byref(nbytes), kid, P(keys), P(out_keys), n, S,
+                                              P(begin_offsets), P(end_offsets), begin_bit, end_bit,
+                                              int(descending), stream)
+
+    with torch.cuda.device(keys.device):
+        _capi.check(call(None), "segmented size query")
+        temp = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=keys.device)
+        _capi.check(call(C.c_void_p(temp.data_ptr())), "cusort segmented sort")
     return out_keys, (out_values if vb else None)
 
 

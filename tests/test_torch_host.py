@@ -88,3 +88,24 @@ def test_sharded_output_capacity():
     _check_output("out_values", torch.empty(64, 2, dtype=torch.int64, device=M), v, 64)
     with pytest.raises(ValueError, match="out_values"):
         _check_output("out_values", torch.empty(128, dtype=torch.int64, device=M), v, 64)
+
+
+def test_segment_offsets_checks():
+    from libcusort_b200.torch_sort import _check_offsets
+    k = _k(10)
+    b = torch.empty(4, dtype=torch.int64, device=M)
+    assert _check_offsets(k, b, b) == 4
+    with pytest.raises(ValueError, match="begin_offsets"):
+        _check_offsets(k, torch.empty(4, dtype=torch.int32, device=M), b)
+    with pytest.raises(ValueError, match="end_offsets"):
+        _check_offsets(k, b, torch.empty(4, dtype=torch.int64))
+    with pytest.raises(ValueError, match="same length"):
+        _check_offsets(k, b, torch.empty(5, dtype=torch.int64, device=M))
+
+
+def test_any_width_payloads_only_where_allowed():
+    k = _k(10)
+    v = torch.empty(10, 3, dtype=torch.int64, device=M)  # 24 bytes per row
+    assert _check_args(k, v, None, None, None, any_width=True) == 24
+    with pytest.raises(ValueError, match="24 bytes"):
+        _check_args(k, v, None, None, None)
