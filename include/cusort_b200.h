@@ -27,8 +27,10 @@
  *     begin_bit > end_bit or end_bit > 8*sizeof(key) (libcusort.cuh:2908).
  *   - Asynchronous on `stream`; no host synchronisation.
  * Differences (stricter): an unknown key type, a value size outside
- * {1,2,4,8,16}, a NULL temp_storage_bytes pointer, or a temp_storage_bytes
- * below the size this library reported returns cudaErrorInvalidValue.
+ * {1,2,4,8,16}, a NULL temp_storage_bytes pointer, a temp_storage_bytes
+ * below the size this library reported, or a d_temp_storage that is not
+ * 16-byte aligned (cudaMalloc'd memory always is) returns
+ * cudaErrorInvalidValue.
  *
  * All pointers are device pointers, naturally aligned for their element
  * type.  The library allocates no device memory.

@@ -70,6 +70,19 @@ def test_invalid_types():
     assert lib.cusort_sort_keys(None, None, 4, None, None, 1000, 0, 32, None) == INVALID
 
 
+def test_misaligned_temp_is_rejected():
+    # checked on the host before any CUDA call: a temp pointer that is not 16-byte aligned
+    lib = _capi.load()
+    rc, need = _query_keys(4, 100_000, 0, 32)
+    assert rc == 0
+    nb = C.c_size_t(need)
+    assert lib.cusort_sort_keys(C.c_void_p(0x10008), C.byref(nb), 4, C.c_void_p(0x20000), C.c_void_p(0x30000),
+                                100_000, 0, 32, None) == INVALID
+    nb = C.c_size_t(need - 1)  # too small, aligned
+    assert lib.cusort_sort_keys(C.c_void_p(0x10000), C.byref(nb), 4, C.c_void_p(0x20000), C.c_void_p(0x30000),
+                                100_000, 0, 32, None) == INVALID
+
+
 def test_trivial_sizes():
     # in/out form reports 1 byte when a copy is still needed, DoubleBuffer 0
     assert _query_keys(4, 0, 0, 32) == (0, 0)
