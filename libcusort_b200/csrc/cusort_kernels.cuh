@@ -520,6 +520,44 @@ struct WarpCounters<4> : WarpCounters<3> {
     uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
     atomicAdd(cnt + (d >> 1), 1u << ((d & 1u) << 4));
   }
+  // Hot-digit variants.  `hot` is one digit holding a large share of the
+  // pass (from the upfront histogram).  Its lanes would serialize on one
+  // shared word in both the count and the match table, so they find each
+  // other with one ballot instead: the lowest of them adds the group's size,
+  // and the ranking takes the ballot as their peer set and skips the table.
+  __device__ __forceinline__ static void count_key_hot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t hot,
+                                                       uint32_t lt) {
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    const bool h = d == hot;
+    const uint32_t hm = __ballot_sync(0xffffffffu, h);
+    const uint32_t add = (h ? (uint32_t)__popc(hm) : 1u) << ((d & 1u) << 4);
+    dev::atom_add_shared_if(!h || (hm & lt) == 0u, cnt + (d >> 1), add, 0u);
+  }
+  template <int S>
+  __device__ __forceinline__ static uint32_t rank_slot_hot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                           uint32_t lt, uint32_t& prev_word, uint32_t hot) {
+    uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    uint32_t* cnt = base;
+    uint32_t* msk = base + kRadix / 2;
+    const bool h = d == hot;
+    const uint32_t hm = __ballot_sync(0xffffffffu, h);
+    const uint32_t word = (uint32_t)(S % NT) * MASK_WORDS + (d >> 2);
+    if (!h) atomicOr(msk + word, 1u << lane);
+    const uint32_t pl = dev::match_digit_ballot<2>(d);
+    __syncwarp();
+    const uint32_t ph = h ? hm : msk[word];
+    // previous slot's table: read by all lanes before the barrier above (a
+    // hot lane clears the word it would have used: zero either way)
+    if (S > 0) msk[prev_word] = 0u;
+    prev_word = word;
+    const uint32_t peers = h ? hm : (pl & ph);
+    const uint32_t below = __popc(peers & lt);
+    const uint32_t leader = 31u - __clz(peers);
+    const uint32_t sh = (d & 1u) << 4;
+    uint32_t old = dev::atom_add_shared_if(lane == leader, cnt + (d >> 1), (below + 1u) << sh, 0u);
+    old = __shfl_sync(0xffffffffu, old, leader);
+    return ((old >> sh) & 0xffffu) + below;
+  }
 };
 
 // Mode 5: mode 4's counting pre-pass and position counters with the peer set
@@ -648,6 +686,16 @@ struct OnesweepCfg {
 #endif
   static constexpr bool RECOMPUTE_DIGIT =
       CUSORT_RANK_MODE_OF(KB_, VB_) >= 4 && (CUSORT_RECOMPUTE_DIGIT == 2 || (CUSORT_RECOMPUTE_DIGIT == 1 && VB_ == 0));
+  // Hot-digit ranking (WarpCounters<4>::count_key_hot / rank_slot_hot) when
+  // a digit holds more than 1/CUSORT_HOT_SHARE of the pass's items; plain
+  // passes only (the counts come from the upfront histogram).
+#ifndef CUSORT_HOT_DIGIT
+#define CUSORT_HOT_DIGIT 0
+#endif
+#ifndef CUSORT_HOT_SHARE
+#define CUSORT_HOT_SHARE 16
+#endif
+  static constexpr bool HOT = CUSORT_HOT_DIGIT && RANK_MODE == 4 && !ROUTED_ && !SEG_;
   static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
   static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
@@ -787,12 +835,15 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     return true;
   };
 
+  // [12..13]: the pass's hot digit, (count << 8 | digit) as u64, 0 if none
+  unsigned long long* s_hot = reinterpret_cast<unsigned long long*>(s_misc + 12);
   if (tid == 0) {
     dev::mbar_init(s_mbar, 1);
     dev::mbar_init(s_mbar + 1, 1);
     dev::fence_mbar_init();
     s_misc[2] = 0;
     s_misc[3] = 0;
+    *s_hot = 0ull;
   }
   dev::pdl_wait();
   dev::pdl_launch_dependents();
@@ -838,6 +889,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       Off pre = 0;
       for (uint32_t w = 0; w < warp; ++w) pre += s_goff[w];
       s_gbase[tid] = pre + incl - cv;
+      if constexpr (CFG::HOT) {
+        if ((uint64_t)cv * CUSORT_HOT_SHARE > a.n) atomicMax(s_hot, ((unsigned long long)cv << 8) | tid);
+      }
     }
   }
   uint32_t cur = s_misc[0];
@@ -982,9 +1036,18 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
     uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
     constexpr bool EARLY = CFG::RANK_MODE >= 4;
+    // the pass's hot digit (256: none); written before the first tile's barrier
+    const uint32_t hot = (CFG::HOT && *s_hot != 0ull) ? (uint32_t)(*s_hot & 0xffu) : 256u;
     if constexpr (EARLY) {
+      if (CFG::HOT && hot < 256u) {
+        if constexpr (CFG::HOT) {
 #pragma unroll
-      for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
+          for (int s = 0; s < KPT; ++s) WC::count_key_hot(s_wtab, warp, RECOMP ? digit_at(s) : dr[s], hot, lt);
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
+      }
     } else {
       static_assert(!RECOMP, "digit recomputation needs the early-count rank modes");
       uint32_t prev = 0;
@@ -1026,10 +1089,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     auto reorder = [&]() {
       if constexpr (EARLY) {
         // rank against the per-warp position counters, store at once
-        uint32_t prev = 0;
-        static_for<0, KPT>([&](auto sc) {
+        auto store = [&](auto sc, uint32_t pos) {
           constexpr int S = decltype(sc)::value;
-          const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev);
           if constexpr (CFG::PACKED_KV) {
             s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
           } else {
@@ -1037,7 +1098,21 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
             if constexpr (VREG) s_vals[pos] = val[S];
             if constexpr (CFG::VSMEM) s_vsort[pos] = s_vals[wfirst_c + S * 32 + lane];
           }
-        });
+        };
+        uint32_t prev = 0;
+        if (CFG::HOT && hot < 256u) {
+          if constexpr (CFG::HOT) {
+            static_for<0, KPT>([&](auto sc) {
+              constexpr int S = decltype(sc)::value;
+              store(sc, WC::template rank_slot_hot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev, hot));
+            });
+          }
+        } else {
+          static_for<0, KPT>([&](auto sc) {
+            constexpr int S = decltype(sc)::value;
+            store(sc, WC::template rank_slot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev));
+          });
+        }
       } else {
 #pragma unroll
         for (int s = 0; s < KPT; ++s) {
