@@ -1039,14 +1039,12 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     // the pass's hot digit (256: none); written before the first tile's barrier
     const uint32_t hot = (CFG::HOT && *s_hot != 0ull) ? (uint32_t)(*s_hot & 0xffu) : 256u;
     if constexpr (EARLY) {
-      if (CFG::HOT && hot < 256u) {
-        if constexpr (CFG::HOT) {
-#pragma unroll
-          for (int s = 0; s < KPT; ++s) WC::count_key_hot(s_wtab, warp, RECOMP ? digit_at(s) : dr[s], hot, lt);
-        }
-      } else {
+      if (__builtin_expect(!CFG::HOT || hot >= 256u, 1)) {
 #pragma unroll
         for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
+      } else if constexpr (CFG::HOT) {
+#pragma unroll
+        for (int s = 0; s < KPT; ++s) WC::count_key_hot(s_wtab, warp, RECOMP ? digit_at(s) : dr[s], hot, lt);
       }
     } else {
       static_assert(!RECOMP, "digit recomputation needs the early-count rank modes");
@@ -1100,17 +1098,15 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
           }
         };
         uint32_t prev = 0;
-        if (CFG::HOT && hot < 256u) {
-          if constexpr (CFG::HOT) {
-            static_for<0, KPT>([&](auto sc) {
-              constexpr int S = decltype(sc)::value;
-              store(sc, WC::template rank_slot_hot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev, hot));
-            });
-          }
-        } else {
+        if (__builtin_expect(!CFG::HOT || hot >= 256u, 1)) {
           static_for<0, KPT>([&](auto sc) {
             constexpr int S = decltype(sc)::value;
             store(sc, WC::template rank_slot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev));
+          });
+        } else if constexpr (CFG::HOT) {
+          static_for<0, KPT>([&](auto sc) {
+            constexpr int S = decltype(sc)::value;
+            store(sc, WC::template rank_slot_hot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev, hot));
           });
         }
       } else {
