@@ -154,22 +154,46 @@ def traffic_from_profiles(workload: str):
 
 
 class Sorter:
-    """One SortPairs/SortKeys call through a C ABI (ours or the reference's)."""
+    """One SortPairs/SortKeys call through a C ABI (ours or the reference's).
+
+    api="raw": the in/out-pointer form (inputs never written).  api="db": the
+    DoubleBuffer form over (keys_in, keys_out) and (vals_in, vals_out); every
+    call starts from selector 0, so the caller restores keys_in / vals_in
+    before each call (the form clobbers both buffers)."""
 
     def __init__(self, impl, torch, kt_name, kid, kb, vb, n, keys_in, keys_out, vals_in, vals_out, stream,
-                 descending=False, begin_bit=0, end_bit=None):
+                 descending=False, begin_bit=0, end_bit=None, api="raw"):
         self.torch = torch
         self.impl = impl
         self.n = n
+        self.api = api
         s = C.c_void_p(stream)
         kin, kout = C.c_void_p(keys_in.data_ptr()), C.c_void_p(keys_out.data_ptr())
         vin = C.c_void_p(vals_in.data_ptr()) if vb else None
         vout = C.c_void_p(vals_out.data_ptr()) if vb else None
         bb, eb = begin_bit, (8 * kb if end_bit is None else end_bit)
+        self.sel = (0, 0)  # DoubleBuffer selectors after the last call
         if impl == "ours":
             from libcusort_b200 import _capi
             lib = _capi.load()
-            if vb:
+            if api == "db":
+                kdb, vdb = _capi.DoubleBufferC(), _capi.DoubleBufferC()
+                kdb.d_buffers[0], kdb.d_buffers[1] = kin.value, kout.value
+                if vb:
+                    vdb.d_buffers[0], vdb.d_buffers[1] = vin.value, vout.value
+
+                def call(t, tb):
+                    kdb.selector, vdb.selector = 0, 0
+                    if vb:
+                        fn = lib.cusort_sort_pairs_descending_db if descending else lib.cusort_sort_pairs_db
+                        rc = fn(t, C.byref(tb), kid, C.byref(kdb), vb, C.byref(vdb), n, bb, eb, s)
+                    else:
+                        fn = lib.cusort_sort_keys_descending_db if descending else lib.cusort_sort_keys_db
+                        rc = fn(t, C.byref(tb), kid, C.byref(kdb), n, bb, eb, s)
+                    self.sel = (kdb.selector, vdb.selector)
+                    return rc
+                self.call = call
+            elif vb:
                 fn = lib.cusort_sort_pairs_descending if descending else lib.cusort_sort_pairs
                 self.call = lambda t, tb: fn(t, C.byref(tb), kid, kin, kout, vb, vin, vout, n, bb, eb, s)
             else:
@@ -182,8 +206,14 @@ class Sorter:
             fn = getattr(rl, f"ref_sort_k{kid}")
             ks, vs = C.c_int(0), C.c_int(0)
             dflag = int(bool(descending))
-            self.call = lambda t, tb: fn(vb, dflag, 1, t, C.byref(tb), kin, kout, C.byref(ks), vin, vout,
-                                         C.byref(vs), n, bb, eb, s)
+            raw = 1 if api == "raw" else 0
+
+            def call(t, tb):
+                ks.value, vs.value = 0, 0
+                rc = fn(vb, dflag, raw, t, C.byref(tb), kin, kout, C.byref(ks), vin, vout, C.byref(vs), n, bb, eb, s)
+                self.sel = (ks.value, vs.value)
+                return rc
+            self.call = call
         tb = C.c_size_t(0)
         rc = self.call(None, tb)
         if rc != 0:
@@ -217,6 +247,43 @@ def time_steps(torch, fn, steps: int, warmup: int, dist=None):
     return a.elapsed_time(b)
 
 
+def time_restored(torch, restore, fn, steps: int, warmup: int):
+    """Mean ms per call of fn() when every call needs its inputs restored first
+    (the DoubleBuffer form clobbers both buffers): restore() runs outside the
+    timed interval, and CUDA events on the launching stream bracket each call."""
+    for _ in range(warmup):
+        restore()
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        restore()
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+
+def verify_index_pairs(torch, keys_in, ko, vo, unsigned=False):
+    """Checks a SortPairs output whose input values were the original indices:
+    keys ascending, values a permutation of 0..n-1, every value carrying its
+    own key (keys_in[value] == key) and stability (inside each run of equal
+    keys the values strictly increase)."""
+    k = ko.view(torch.int32)
+    n = k.numel()
+    if unsigned:
+        k = k ^ torch.tensor(-(2 ** 31), dtype=torch.int32, device=k.device)
+    idx = vo.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    out = {"sorted": bool((k[1:] >= k[:-1]).all().item())}
+    out["permutation"] = bool(torch.equal(torch.sort(idx).values, torch.arange(n, device=idx.device)))
+    out["values_carry_keys"] = bool(torch.equal(keys_in.view(torch.int32)[idx], ko.view(torch.int32)))
+    eq = k[1:] == k[:-1]
+    out["stable"] = bool((idx[1:][eq] > idx[:-1][eq]).all().item())
+    out["equal_key_pairs_checked"] = int(eq.sum().item())
+    return out
+
+
 def e2e_measure(torch, sorter_factory, n, kb, vb, keys_host, vals_host, steps, warmup, device):
     """Host buffers: per step H2D (keys, values), sort, D2H (sorted keys, values)."""
     kin = torch.empty(n * kb, dtype=torch.uint8, device=device)
@@ -241,33 +308,37 @@ def e2e_measure(torch, sorter_factory, n, kb, vb, keys_host, vals_host, steps, w
 
 
 def cpu_baseline(seconds: float, n_full: int):
-    """Oracle parallel stable sort of int32/uint32 pairs on all host cores, bounded sample."""
+    """Oracle parallel stable sort of int32/uint32 pairs on all host cores, on the FULL workload
+    size (whole sorts repeated until about `seconds` have passed); a one-thread row on a 2^24
+    sample beside it."""
     from oracle import oracle as O
     cores = os.cpu_count() or 1
     rng = np.random.default_rng(2)
-    m = min(n_full, 1 << 22)
+    m = n_full
     keys = rng.integers(-(2 ** 31), 2 ** 31, size=m, dtype=np.int64).astype(np.int32)
     vals = np.arange(m, dtype=np.uint32)
     reps, t_total = 0, 0.0
-    while t_total < seconds and reps < 1000:
+    while (t_total < seconds or reps < 2) and reps < 1000:
         t0 = time.perf_counter()
         O.oracle_sort("i32", keys, vals, 0, 32, False, threads=cores)
         t_total += time.perf_counter() - t0
         reps += 1
     rate = reps * m / t_total / 1e9
-    # one-thread std::stable_sort of the same sample, bounded to about a fifth of the time
+    # one-thread std::stable_sort on a 2^24 sample, bounded to about a fifth of the time
+    m1 = min(m, 1 << 24)
     reps1, t1 = 0, 0.0
-    while t1 < seconds / 5 and reps1 < 100:
+    while (t1 < seconds / 5 or reps1 < 1) and reps1 < 100:
         t0 = time.perf_counter()
-        O.oracle_sort("i32", keys, vals, 0, 32, False, threads=1)
+        O.oracle_sort("i32", keys[:m1], vals[:m1], 0, 32, False, threads=1)
         t1 += time.perf_counter() - t0
         reps1 += 1
     return {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{reps} x {m} int32/uint32 pairs (2^{m.bit_length() - 1}), __gnu_parallel::stable_sort "
-                      f"over {cores} OpenMP threads, {t_total:.1f} s",
+            "sample": f"{reps} x {m} int32/uint32 pairs (2^{m.bit_length() - 1}, the full workload), "
+                      f"__gnu_parallel::stable_sort over {cores} OpenMP threads, {t_total:.1f} s",
             "cpu_model": cpu_model(),
-            "single_thread": {"value": reps1 * m / t1 / 1e9, "unit": UNIT, "cores": 1,
-                              "sample": f"{reps1} x {m} pairs, std::stable_sort, {t1:.1f} s"}}
+            "single_thread": {"value": reps1 * m1 / t1 / 1e9, "unit": UNIT, "cores": 1,
+                              "sample": f"{reps1} x {m1} pairs (2^{m1.bit_length() - 1} sample), "
+                                        f"std::stable_sort, {t1:.1f} s"}}
 
 
 def cpu_model():
@@ -305,11 +376,8 @@ def run_single(args, torch, dist=None, rank=0, world=1):
     ms_step = ms / args.steps
     value = n / (ms_step * 1e-3) / 1e9
 
-    # correctness spot check of the timed output (sortedness + permutation checksum)
-    ko = kout.view(torch.int32)
-    ok_sorted = bool((ko[1:] >= ko[:-1]).all().item())
-    vo = vout.view(torch.int32)
-    ok_stable = bool(torch.equal(keys[vo.long()], ko)) if ok_sorted else False
+    # check of the timed output: sorted, permutation, values carry their keys, stable
+    verified = verify_index_pairs(torch, keys, kout, vout)
 
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -319,7 +387,7 @@ def run_single(args, torch, dist=None, rank=0, world=1):
         "config": {"workload": "configs[1]: SortPairs 2^26 int32 keys uniform + uint32 index values", "n": n,
                    "key": "int32", "value_bytes": 4, "api": "in/out pointers (cusort_sort_pairs)",
                    "l2": "inputs 512 MiB > 126 MB L2 (no flush needed)"},
-        "verified": {"sorted": ok_sorted, "values_match_keys": ok_stable},
+        "verified": verified,
         "clocks": clocks,
     }
     if args.impl == "ours":
@@ -345,7 +413,11 @@ def run_single(args, torch, dist=None, rank=0, world=1):
         traffic = traffic_from_profiles("i32_u32_pairs_2^26")
         out["roofline"] = {"bound": "hbm", "kernel": "onesweep_kernel", "achieved": achieved, "peak": peak,
                            "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
-                           "traffic": traffic, "algorithmic_bytes_per_launch": alg,
+                           "traffic": traffic,
+                           "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one onesweep launch "
+                                             "from the committed ncu capture (profiles/onesweep_traffic.json), not "
+                                             "measured in this run",
+                           "algorithmic_bytes_per_launch": alg,
                            "launch_ms": os_ms, "histogram_launch_ms": h_ms,
                            "histogram_gbs": n * kb / (h_ms * 1e-3) / 1e9,
                            "whole_sort_frac": (4 * alg / (ms_step * 1e-3) / 1e9) / peak}
@@ -363,6 +435,7 @@ def run_single(args, torch, dist=None, rank=0, world=1):
                   "path": "pinned host -> H2D -> sort (C ABI) -> D2H -> pinned host"}
     if not args.no_secondary:
         out["secondary"] = secondary(args, torch, device)
+        out["secondary"]["double_buffer_api_2^26"] = double_buffer_forms(args, torch, device)
         out["secondary"]["other_configs_2^26"] = other_configs(args, torch, device)
         out["secondary"]["configs[0]_u32_keys_2^20_hot_l2"] = small_hot_l2(args, torch, device)
         if args.impl == "ours":
@@ -376,6 +449,41 @@ def run_single(args, torch, dist=None, rank=0, world=1):
                                          "libcusort.cuh 1.0.1 built for sm_100a (nvcc 12.9, default build) on the "
                                          "same B200, full workload"}
     return out
+
+
+def double_buffer_forms(args, torch, device):
+    """The DoubleBuffer API form (each library's fastest: no staging buffers) of the two headline
+    workloads: 2^26 int32 keys + uint32 index values, and 2^26 uint32 keys-only.  The inputs are
+    restored from a pristine copy before every call (outside the timed interval); CUDA events
+    bracket each call; 3 warm-up + 10 timed calls.  The pairs output of the last call is checked
+    (sorted, permutation, values carry their keys, stable)."""
+    n = 1 << args.log2n
+    stream = torch.cuda.current_stream().cuda_stream
+    res = {}
+    keys, vals = make_inputs(torch, n, seed=2, device=device)
+    kbuf, vbuf = keys.clone(), vals.clone()
+    k_alt, v_alt = torch.empty_like(keys), torch.empty_like(vals)
+    s = Sorter(args.impl, torch, "i32", 5, 4, 4, n, kbuf, k_alt, vbuf, v_alt, stream, api="db")
+
+    def restore():
+        kbuf.copy_(keys)
+        vbuf.copy_(vals)
+    ms = time_restored(torch, restore, s, 10, 3)
+    ks, vs = s.sel
+    res["i32_u32_pairs_2^26"] = {"ms_per_step": round(ms, 4), "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2),
+                                 "verified": verify_index_pairs(torch, keys, (kbuf, k_alt)[ks], (vbuf, v_alt)[vs])}
+    del s, kbuf, vbuf, k_alt, v_alt, vals
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    ukeys = torch.randint(0, 256, (n * 4,), dtype=torch.uint8, device=device, generator=g)
+    kbuf, k_alt = ukeys.clone(), torch.empty_like(ukeys)
+    dummy = torch.empty(1, dtype=torch.uint8, device=device)
+    s = Sorter(args.impl, torch, "u32", 4, 4, 0, n, kbuf, k_alt, dummy, dummy, stream, api="db")
+    ms = time_restored(torch, lambda: kbuf.copy_(ukeys), s, 10, 3)
+    ko = (kbuf, k_alt)[s.sel[0]].view(torch.int32) ^ torch.tensor(-(2 ** 31), dtype=torch.int32, device=device)
+    res["u32_keys_only_2^26"] = {"ms_per_step": round(ms, 4), "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2),
+                                 "sorted": bool((ko[1:] >= ko[:-1]).all().item())}
+    return res
 
 
 def secondary(args, torch, device):
