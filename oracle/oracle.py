@@ -19,6 +19,8 @@ bench.py's cpu_baseline / reference legs -- never by the libcusort_b200 product.
 from __future__ import annotations
 
 import ctypes as C
+import json
+import os
 import subprocess
 from pathlib import Path
 
@@ -37,9 +39,35 @@ _oracle = None
 _ref = None
 
 
+def reference_dir() -> Path | None:
+    """Checkout of the reference library (the directory holding libcusort.cuh), needed only to
+    BUILD oracle/_ref: the environment variable CUSORT_REFERENCE_DIR, else the "reference_path"
+    field of BASELINE.json at the repository root.  None when neither names a directory that
+    holds libcusort.cuh (the GPU box only uses the prebuilt library)."""
+    cand = os.environ.get("CUSORT_REFERENCE_DIR")
+    if not cand:
+        meta = HERE.parent / "BASELINE.json"
+        if meta.exists():
+            try:
+                cand = json.loads(meta.read_text()).get("reference_path")
+            except (ValueError, OSError):
+                cand = None
+    if cand and (Path(cand) / "libcusort.cuh").exists():
+        return Path(cand)
+    return None
+
+
 def build(ref: bool = True) -> None:
-    targets = ["oracle"] + (["ref"] if ref else [])
-    subprocess.run(["make", "-s", "-j8", *targets], cwd=HERE, check=True)
+    """make the oracle (and, with ref=True and a reference checkout, oracle/_ref)."""
+    targets = ["oracle"]
+    extra = []
+    if ref:
+        rd = reference_dir()
+        if rd is None:
+            raise RuntimeError("building oracle/_ref needs the reference checkout: set CUSORT_REFERENCE_DIR")
+        targets.append("ref")
+        extra.append(f"REF_DIR={rd}")
+    subprocess.run(["make", "-s", "-j8", *targets, *extra], cwd=HERE, check=True)
 
 
 def _load_oracle():
