@@ -147,10 +147,15 @@ cudaError_t cusort_sort_pairs_wide(void* d_temp_storage, size_t* temp_storage_by
  *     1 KiB per tile (2 KiB from 2^30 items on) plus a few KiB, a tile being
  *     4096 to 18432 items by key and value width (e.g. 2^26 32-bit keys, or
  *     2^25 32-bit keys with 32-bit values, fit in 4 MiB).
- *   - The array occupies CUSORT_NOALLOC_SCRATCH_BYTES on every GPU where this
- *     entry point has run, until the process exits.
+ *   - The array occupies CUSORT_NOALLOC_SCRATCH_BYTES on every GPU whose
+ *     context loads this library's device code, until the process exits:
+ *     under lazy module loading (the CUDA default) only once this entry point
+ *     has run there; with CUDA_MODULE_LOADING=EAGER on every GPU that uses
+ *     the library at all.
  *   - The first call on each device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     (cudaGetSymbolAddress) and keeps it; make that first call before any
+ *     stream capture.  A device reset (cudaDeviceReset) between calls is not
+ *     supported: the kept address would belong to the old context.
  *   - All calls share the one array and it keeps the last call's contents:
  *     calls whose GPU work can overlap (other streams, other host threads on
  *     the same device) race on it and corrupt each other's results, so
@@ -213,10 +218,26 @@ cudaError_t cusort_segmented_sort_pairs(void* d_temp_storage, size_t* temp_stora
  *   rank's receive total.  Returns 0 on success.
  * cusort_mgpu_sort: two-phase temp protocol as the single-GPU calls (the size
  *   depends on the communicator's size, n_local and out_capacity).  It
- *   synchronises `stream` once (to read the gathered counts).  Returns
+ *   waits on the host once (for the gathered counts).  Returns
  *   cudaErrorInvalidValue on every rank, before any data exchange, when some
  *   rank's share would exceed out_capacity.  *n_out receives this rank's
- *   item count.  value_bytes 0 = keys only. */
+ *   item count.  value_bytes 0 = keys only.
+ *
+ * Failure handling (no reference counterpart: the reference is single-GPU and
+ * its only wait is an unbounded lookback spin, libcusort.cuh:1360-1374).  The
+ * communicator is non-blocking and every host wait of the library is bounded
+ * by the communicator's limit (default 30 s): joining in
+ * cusort_mgpu_comm_init, the gathered counts inside cusort_mgpu_sort, each
+ * NCCL call being issued, and cusort_mgpu_wait.  When a limit passes or NCCL
+ * reports an asynchronous error (a rank that left, a broken connection), the
+ * communicator is aborted (ncclCommAbort: NCCL kernels still waiting for a
+ * peer give up), the call returns cudaErrorTimeout (or the mapped NCCL
+ * error), every later call on that communicator returns cudaErrorTimeout at
+ * once, and cusort_mgpu_comm_destroy only frees the handle.
+ * cusort_mgpu_set_timeout_ns: that limit, per communicator.
+ * cusort_mgpu_wait: bounded host wait for all work queued on `stream` so far
+ *   (the exchange's fence collective and the local sort included); use it in
+ *   place of cudaStreamSynchronize to learn of a peer's failure. */
 cudaError_t cusort_mgpu_unique_id(unsigned char* id128);
 cudaError_t cusort_mgpu_comm_init(void** comm, const unsigned char* id128, int nranks, int rank);
 cudaError_t cusort_mgpu_comm_destroy(void* comm);
@@ -226,6 +247,18 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp_storage, size_t* temp_stor
                              size_t value_bytes, const void* d_keys_in, const void* d_values_in, int64_t n_local,
                              void* d_keys_out, void* d_values_out, int64_t out_capacity, int64_t* n_out,
                              int begin_bit, int end_bit, int descending, cudaStream_t stream);
+cudaError_t cusort_mgpu_set_timeout_ns(void* comm, uint64_t ns);
+cudaError_t cusort_mgpu_wait(void* comm, cudaStream_t stream);
+
+/* Phase times of this host thread's last cusort_mgpu_sort call, measured with
+ * CUDA events on its stream while timing is on (cusort_mgpu_set_timing(1), per
+ * host thread; returns the previous setting).  With timing on, each call
+ * waits for its own last phase before returning.  cusort_mgpu_get_phase_times
+ * fills up to `capacity` (ms, name) pairs -- names are static strings such as
+ * "counts+gather", "host", "routed-pass", "exchange", "local-sort" -- and
+ * returns how many it filled. */
+int cusort_mgpu_set_timing(int enable);
+int cusort_mgpu_get_phase_times(float* ms, const char** names, int capacity);
 
 /* ---- library state, status and diagnostics (no reference counterpart;
  *      the reference has compile-time macros only, libcusort.cuh:119-148) -- */

@@ -19,7 +19,9 @@
 namespace {
 
 // The scratch itself: CUSORT_NOALLOC_SCRATCH_BYTES on every GPU whose context
-// loads this module, held until the process exits.  Host code must not use
+// loads this module (under lazy loading, once this entry point runs there; with
+// CUDA_MODULE_LOADING=EAGER, on every GPU that uses the library), held until
+// the process exits.  Host code must not use
 // the array's name as a device pointer: on the host it only names a stand-in,
 // so its device address is looked up with cudaGetSymbolAddress below.
 __device__ __align__(256) unsigned char g_noalloc_scratch[CUSORT_NOALLOC_SCRATCH_BYTES];
@@ -35,7 +37,9 @@ std::map<int, void*>& scratch_addresses() {
 
 // Device address of the scratch on the current device, looked up once per
 // device (the first call on a device does this; it must not be inside a
-// stream capture).
+// stream capture) and kept for the life of the process.  A cudaDeviceReset
+// between calls is therefore not supported: the module would be loaded again
+// in a new context and the kept address could be stale.
 cudaError_t scratch_on_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -3,10 +3,12 @@
 It exists for callers that cannot allocate device memory when they sort (an
 allocator hook sorting its own free lists, a plugin whose host process has
 reserved all device memory, a latency-bound loop that must not let cudaMalloc
-synchronise the device).  It must give the same results as the ordinary
-DoubleBuffer entry points, which take caller temp storage, including on a
-second call that reuses the library's scratch array, and must refuse sizes
-that do not fit that array.  This file is collected last on purpose.
+synchronise the device).  Its results must equal the CPU oracle's (a stable
+sort, bit for bit) and the ordinary DoubleBuffer entry points' (which take
+caller temp storage, selectors included), also on a second call that reuses
+the library's scratch array; a call must leave the device's free memory
+unchanged; and sizes that do not fit the array must be refused.  This file is
+collected last on purpose.
 """
 from __future__ import annotations
 
@@ -18,6 +20,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 from libcusort_b200 import _capi  # noqa: E402
+from oracle import oracle as O  # noqa: E402
 from tests import datagen as D  # noqa: E402
 from tests.gpu_helpers import DevBuf, run_ours, same_bits  # noqa: E402
 
@@ -59,26 +62,54 @@ def sort_noalloc(kt, keys, values=None, begin_bit=0, end_bit=None, descending=Fa
     return rc, ko, vo, kdb.selector, vdb.selector
 
 
-def test_no_alloc_matches_allocating_entry_points_on_two_calls():
+def test_no_alloc_matches_oracle_on_two_calls():
     # Two calls in a row: the second reuses (and must re-clear) the scratch.
-    cases = [("i32", 1 << 20, 4, False, 0, 32, 11), ("f64", 300_001, 16, True, 3, 61, 12)]
+    cases = [("i32", 1 << 20, 4, False, 0, 32, 11), ("f64", 300_001, 16, True, 3, 61, 12),
+             ("i32", 1 << 20, 4, False, 0, 32, 14)]
     for kt, n, vb, desc, b, e, seed in cases:
         keys = D.special_floats(kt, n, seed=seed) if kt.startswith("f") else D.uniform_bits(kt, n, seed=seed)
         vals = D.values_for(n, vb)
+        ek, ev = O.oracle_sort(kt, keys, vals, b, e, desc)
         rc, ko, vo, ks, vs = sort_noalloc(kt, keys, vals, b, e, desc)
         assert rc == 0
-        ek, ev, info = run_ours(kt, keys, vals, b, e, desc, api="db")
-        assert same_bits(ko, ek) and same_bits(vo, ev)
+        assert same_bits(ko, ek) and same_bits(vo, ev), f"differs from the oracle ({kt}, n={n})"
+        # same selector updates as the allocating DoubleBuffer entry point
+        _, _, info = run_ours(kt, keys, vals, b, e, desc, api="db")
         assert (ks, vs) == (info["ksel"], info["vsel"])
 
 
-def test_no_alloc_keys_only_matches():
+def test_no_alloc_keys_only_matches_oracle():
     keys = D.uniform_bits("u32", 2_000_000, seed=13)
+    ek, _ = O.oracle_sort("u32", keys, None, 0, 20)
     for _ in range(2):
         rc, ko, _, ks, _ = sort_noalloc("u32", keys, None, 0, 20)
         assert rc == 0
-        ek, _, info = run_ours("u32", keys, None, 0, 20, api="db")
-        assert same_bits(ko, ek) and ks == info["ksel"]
+        assert same_bits(ko, ek)
+        assert ks == 1  # 3 passes flip the selector once per pass
+
+
+def test_no_alloc_call_leaves_free_memory_unchanged():
+    lib = _capi.load()
+    n = 1 << 20
+    keys = D.uniform_bits("i32", n, seed=21)
+    vals = D.values_for(n, 4)
+    k0, k1 = DevBuf.from_array(keys), DevBuf(keys.nbytes)
+    v0, v1 = DevBuf.from_array(vals), DevBuf(vals.nbytes)
+    kdb, vdb = _capi.DoubleBufferC(), _capi.DoubleBufferC()
+
+    def call():
+        kdb.d_buffers[0], kdb.d_buffers[1], kdb.selector = k0.ptr.value, k1.ptr.value, 0
+        vdb.d_buffers[0], vdb.d_buffers[1], vdb.selector = v0.ptr.value, v1.ptr.value, 0
+        rc = lib.cusort_sort_db_noalloc(_capi.KEY_TYPES["i32"], C.byref(kdb), 4, C.byref(vdb), n, 0, 32, 0,
+                                        _stream())
+        torch.cuda.synchronize()
+        return rc
+
+    assert call() == 0  # warm-up: the first call may load the library's device code
+    free0, _ = torch.cuda.mem_get_info()
+    assert call() == 0
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"free device memory changed across a call: {free0} -> {free1}"
 
 
 def test_no_alloc_rejects_sizes_beyond_the_scratch():
