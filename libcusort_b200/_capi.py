@@ -19,6 +19,7 @@ KEY_BYTES = {"u8": 1, "i8": 1, "u16": 2, "i16": 2, "u32": 4, "i32": 4, "u64": 8,
 
 CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
+CUDA_ERROR_TIMEOUT = 909  # cudaErrorTimeout
 
 # Every sort/utility symbol the header declares, with (restype, argtypes).
 _vp, _sz, _i64, _i, _u32, _u64 = C.c_void_p, C.c_size_t, C.c_int64, C.c_int, C.c_uint32, C.c_uint64
@@ -53,6 +54,10 @@ SIGNATURES = {
                               C.POINTER(_i64)]),
     "cusort_mgpu_sort": (_i, [_vp, _vp, _P_SZ, _i, _sz, _vp, _vp, _i64, _vp, _vp, _i64, C.POINTER(_i64), _i, _i,
                               _i, _vp]),
+    "cusort_mgpu_set_timeout_ns": (_i, [_vp, _u64]),
+    "cusort_mgpu_wait": (_i, [_vp, _vp]),
+    "cusort_mgpu_set_timing": (_i, [_i]),
+    "cusort_mgpu_get_phase_times": (_i, [C.POINTER(C.c_float), C.POINTER(C.c_char_p), _i]),
     "cusort_version": (C.c_char_p, []),
     "cusort_set_launch_mode": (_i, [_i]),
     "cusort_read_device_status": (_i, [_vp, C.POINTER(_u32), _vp]),

@@ -31,6 +31,8 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <time.h>
+
 #include <algorithm>
 #include <cstddef>
 #include <cstdio>
@@ -83,6 +85,12 @@ thread_local PinnedCounts g_pinned_counts;
 // the communicator is destroyed).
 struct MgpuComm {
   ncclComm_t nccl = nullptr;
+  // Bound on every host wait of a call (the gathered counts, a non-blocking
+  // NCCL call being issued, cusort_mgpu_wait); on expiry the communicator is
+  // aborted and the call returns cudaErrorTimeout.
+  uint64_t timeout_ns = 30000000000ull;
+  bool aborted = false;  // after ncclCommAbort: every later call fails at once
+  cudaEvent_t done = nullptr;  // cusort_mgpu_wait
   std::map<std::pair<int, std::string>, void*> mapped;  // (peer, IPC handle) -> local address
   // pipelined exchange: copy streams (one per peer, up to kMaxCopyStreams) and events
   std::vector<cudaStream_t> copy_streams;
@@ -90,8 +98,65 @@ struct MgpuComm {
   ~MgpuComm() {
     for (cudaStream_t s : copy_streams) cudaStreamDestroy(s);
     for (cudaEvent_t e : events) cudaEventDestroy(e);
+    if (done) cudaEventDestroy(done);
   }
 };
+
+uint64_t now_ns() {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (uint64_t)ts.tv_sec * 1000000000ull + (uint64_t)ts.tv_nsec;
+}
+
+void pause_briefly() {
+  timespec ts = {0, 20000};  // 20 us between polls
+  nanosleep(&ts, nullptr);
+}
+
+// Ends the communicator after a failed or expired wait: NCCL kernels still
+// waiting for a peer give up, and every later call on it fails at once.
+cudaError_t abort_comm(MgpuComm* mc, cudaError_t why) {
+  if (!mc->aborted) {
+    ncclCommAbort(mc->nccl);
+    mc->aborted = true;
+  }
+  return why;
+}
+
+cudaError_t nccl_to_cuda(ncclResult_t r);
+
+// The communicator is non-blocking: an NCCL call may return ncclInProgress
+// while it is still being issued.  Polls until it has been (bounded), and
+// aborts the communicator on an error or when the limit passes.
+cudaError_t settle(MgpuComm* mc, ncclResult_t r) {
+  if (r != ncclSuccess && r != ncclInProgress) return abort_comm(mc, nccl_to_cuda(r));
+  const uint64_t t0 = now_ns();
+  while (r == ncclInProgress) {
+    if (ncclCommGetAsyncError(mc->nccl, &r) != ncclSuccess) return abort_comm(mc, cudaErrorUnknown);
+    if (r == ncclSuccess) break;
+    if (r != ncclInProgress) return abort_comm(mc, nccl_to_cuda(r));
+    if (now_ns() - t0 > mc->timeout_ns) return abort_comm(mc, cudaErrorTimeout);
+    pause_briefly();
+  }
+  return cudaSuccess;
+}
+
+// Host wait for `ev` (work on the stream, NCCL collectives included), bounded
+// by the communicator's limit; an asynchronous NCCL error (a peer that left,
+// a broken connection) or the limit aborts the communicator.
+cudaError_t wait_event(MgpuComm* mc, cudaEvent_t ev) {
+  const uint64_t t0 = now_ns();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return cudaSuccess;
+    if (q != cudaErrorNotReady) return q;
+    ncclResult_t st = ncclSuccess;
+    if (ncclCommGetAsyncError(mc->nccl, &st) != ncclSuccess) return abort_comm(mc, cudaErrorUnknown);
+    if (st != ncclSuccess && st != ncclInProgress) return abort_comm(mc, nccl_to_cuda(st));
+    if (now_ns() - t0 > mc->timeout_ns) return abort_comm(mc, cudaErrorTimeout);
+    pause_briefly();
+  }
+}
 
 // Exchange modes, ordered: the call uses the lowest mode any rank asks for.
 enum : unsigned long long { kXchgNccl = 0, kXchgCopy = 1, kXchgRouted = 2, kXchgPipe = 3 };
@@ -187,18 +252,31 @@ cudaError_t peer_address(MgpuComm* c, int peer, const cudaIpcMemHandle_t& h, uns
   return cudaSuccess;
 }
 
-// Phase timing of one call (environment CUSORT_MGPU_TIMING=1): events on the
-// stream at each phase boundary, printed to stderr when the call returns.
+// Phase timing of one call (cusort_mgpu_set_timing(1), per host thread, or
+// environment CUSORT_MGPU_TIMING=1): events on the stream at each phase
+// boundary; when the call returns the host waits for the last one and keeps
+// the phase times for cusort_mgpu_get_phase_times (the environment variable
+// also prints them to stderr).
+thread_local int g_timing = 0;
+struct PhaseRecord {
+  int n = 0;
+  const char* name[8];
+  float ms[8];
+};
+thread_local PhaseRecord g_last_phases;
+
 struct PhaseTimer {
   static constexpr int kMax = 8;
-  bool on = false;
+  bool on = false, print = false;
   cudaStream_t stream = nullptr;
   int n = 0, rank = 0;
   cudaEvent_t ev[kMax];
   const char* name[kMax];
   PhaseTimer(cudaStream_t s, int r) : stream(s), rank(r) {
     const char* v = std::getenv("CUSORT_MGPU_TIMING");
-    on = v && v[0] == '1';
+    print = v && v[0] == '1';
+    on = print || g_timing;
+    if (on) g_last_phases.n = 0;
   }
   void mark(const char* what) {
     if (!on || n >= kMax) return;
@@ -210,13 +288,19 @@ struct PhaseTimer {
   ~PhaseTimer() {
     if (!on || n == 0) return;
     if (cudaEventSynchronize(ev[n - 1]) == cudaSuccess) {
-      std::fprintf(stderr, "cusort_mgpu rank %d:", rank);
+      g_last_phases.n = n - 1;
       for (int i = 1; i < n; ++i) {
         float ms = 0.f;
         cudaEventElapsedTime(&ms, ev[i - 1], ev[i]);
-        std::fprintf(stderr, " %s %.3f", name[i], ms);
+        g_last_phases.name[i - 1] = name[i];
+        g_last_phases.ms[i - 1] = ms;
       }
-      std::fprintf(stderr, " (ms)\n");
+      if (print) {
+        std::fprintf(stderr, "cusort_mgpu rank %d:", rank);
+        for (int i = 0; i < g_last_phases.n; ++i)
+          std::fprintf(stderr, " %s %.3f", g_last_phases.name[i], g_last_phases.ms[i]);
+        std::fprintf(stderr, " (ms)\n");
+      }
     }
     for (int i = 0; i < n; ++i) cudaEventDestroy(ev[i]);
   }
@@ -369,21 +453,76 @@ cudaError_t cusort_mgpu_comm_init(void** comm, const unsigned char* id, int nran
   if (!comm || !id || nranks < 1 || rank < 0 || rank >= nranks) return cudaErrorInvalidValue;
   ncclUniqueId u;
   std::memcpy(&u, id, sizeof(u));
+  // Non-blocking communicator: every wait on it is bounded (settle,
+  // wait_event) and can end in ncclCommAbort.
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
   ncclComm_t c = nullptr;
-  ncclResult_t r = ncclCommInitRank(&c, nranks, u, rank);
-  if (r != ncclSuccess) return nccl_to_cuda(r);
+  ncclResult_t r = ncclCommInitRankConfig(&c, nranks, u, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    if (c) ncclCommAbort(c);
+    return nccl_to_cuda(r);
+  }
   MgpuComm* mc = new MgpuComm();
   mc->nccl = c;
+  const cudaError_t e = settle(mc, r);  // every rank must join within the limit
+  if (e != cudaSuccess) {
+    delete mc;
+    return e;
+  }
   *comm = mc;
   return cudaSuccess;
+}
+
+cudaError_t cusort_mgpu_set_timeout_ns(void* comm, uint64_t ns) {
+  if (!comm || ns == 0) return cudaErrorInvalidValue;
+  static_cast<MgpuComm*>(comm)->timeout_ns = ns;
+  return cudaSuccess;
+}
+
+cudaError_t cusort_mgpu_wait(void* comm, cudaStream_t stream) {
+  if (!comm) return cudaErrorInvalidValue;
+  MgpuComm* mc = static_cast<MgpuComm*>(comm);
+  if (mc->aborted) return cudaErrorTimeout;
+  if (!mc->done) {
+    const cudaError_t e = cudaEventCreateWithFlags(&mc->done, cudaEventDisableTiming);
+    if (e) return e;
+  }
+  const cudaError_t e = cudaEventRecord(mc->done, stream);
+  if (e) return e;
+  return wait_event(mc, mc->done);
+}
+
+int cusort_mgpu_set_timing(int enable) {
+  const int prev = g_timing;
+  g_timing = enable ? 1 : 0;
+  return prev;
+}
+
+int cusort_mgpu_get_phase_times(float* ms, const char** names, int capacity) {
+  const int m = std::min(g_last_phases.n, std::max(capacity, 0));
+  for (int i = 0; i < m; ++i) {
+    if (ms) ms[i] = g_last_phases.ms[i];
+    if (names) names[i] = g_last_phases.name[i];
+  }
+  return m;
 }
 
 cudaError_t cusort_mgpu_comm_destroy(void* comm) {
   if (!comm) return cudaErrorInvalidValue;
   MgpuComm* mc = static_cast<MgpuComm*>(comm);
-  for (auto& kv : mc->mapped) cudaIpcCloseMemHandle(kv.second);
   for (cudaStream_t st : mc->copy_streams) cudaStreamSynchronize(st);
-  const cudaError_t e = nccl_to_cuda(ncclCommDestroy(mc->nccl));
+  for (auto& kv : mc->mapped) cudaIpcCloseMemHandle(kv.second);
+  cudaError_t e = cudaSuccess;
+  if (!mc->aborted) {
+    // non-blocking communicator: finish outstanding work, then free it
+    ncclResult_t r = ncclCommFinalize(mc->nccl);
+    e = settle(mc, r);
+    if (!mc->aborted) {
+      r = ncclCommDestroy(mc->nccl);
+      if (r != ncclSuccess && r != ncclInProgress) e = nccl_to_cuda(r);
+    }
+  }
   delete mc;
   return e;
 }
@@ -400,6 +539,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   if (begin_bit < 0 || end_bit < 0 || begin_bit > end_bit || end_bit > 8 * kb) return cudaErrorInvalidValue;
   if (n_local < 0 || out_capacity < 0) return cudaErrorInvalidValue;
   MgpuComm* mc = static_cast<MgpuComm*>(comm);
+  if (mc->aborted) return cudaErrorTimeout;
   ncclComm_t nc = mc->nccl;
   int nranks = 0, rank = 0;
   cudaError_t e = nccl_to_cuda(ncclCommCount(nc, &nranks));
@@ -521,7 +661,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
   e = cudaMemcpyAsync(reinterpret_cast<uint8_t*>(rec) + offsetof(RankRecord, hk), h_tail, tail,
                       cudaMemcpyHostToDevice, stream);
   if (e) return e;
-  e = nccl_to_cuda(ncclAllGather(rec, all_rec, sizeof(RankRecord), ncclUint8, nc, stream));
+  e = settle(mc, ncclAllGather(rec, all_rec, sizeof(RankRecord), ncclUint8, nc, stream));
   if (e) return e;
   e = cudaMemcpyAsync(h_all, all_rec, (size_t)nranks * sizeof(RankRecord), cudaMemcpyDeviceToHost, stream);
   if (e) return e;
@@ -568,8 +708,9 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     partitioned = true;
   }
 
-  // 3. plan (identical on every rank)
-  e = cudaEventSynchronize(counts_ready);
+  // 3. plan (identical on every rank); the wait is bounded and aborts the
+  //    communicator when a rank never arrives
+  e = wait_event(mc, counts_ready);
   cudaEventDestroy(counts_ready);
   if (e) return e;
   std::vector<uint64_t> all_counts((size_t)nranks * 256);
@@ -682,7 +823,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     }
     timer.mark("routed-pass");
     if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
-    if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
+    if (!e) e = settle(mc, ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
     if (e) return e;
   } else if (mode == kXchgRouted) {
     // Fused partition + exchange: this rank's items for q go after the items
@@ -724,7 +865,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
     // Fence: once every rank's routed pass (earlier on its stream) is done,
     // the all-reduce completes everywhere and the received data is complete.
     if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
-    if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
+    if (!e) e = settle(mc, ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
     if (e) return e;
   } else {
     if (!partitioned) {
@@ -757,7 +898,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
         so += send[q];
       }
       if (!e) e = cudaMemsetAsync(fence, 0, sizeof(int), stream);
-      if (!e) e = nccl_to_cuda(ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
+      if (!e) e = settle(mc, ncclAllReduce(fence, fence, 1, ncclInt32, ncclSum, nc, stream));
       if (e) return e;
     } else {
       ncclResult_t r = ncclGroupStart();
@@ -776,7 +917,7 @@ cudaError_t cusort_mgpu_sort(void* comm, void* d_temp, size_t* temp_bytes, cusor
         ro += recv[q];
       }
       ncclResult_t r2 = ncclGroupEnd();
-      e = nccl_to_cuda(r != ncclSuccess ? r : r2);
+      e = (r != ncclSuccess && r != ncclInProgress) ? abort_comm(mc, nccl_to_cuda(r)) : settle(mc, r2);
       if (e) return e;
     }
   }

@@ -52,6 +52,31 @@ class ShardedSorter:
             self.lib.cusort_mgpu_comm_destroy(self.comm)
             self.comm = None
 
+    def set_timeout(self, seconds: float) -> None:
+        """Bound on every host wait of this communicator (default 30 s); on expiry the
+        communicator is aborted and the call raises CusortError (cudaErrorTimeout)."""
+        _capi.check(self.lib.cusort_mgpu_set_timeout_ns(self.comm, int(seconds * 1e9)), "cusort_mgpu_set_timeout_ns")
+
+    def wait(self) -> None:
+        """Bounded wait for everything queued on the current stream (the exchange fence and the
+        local sort included); raises CusortError if a peer failed or the limit passed."""
+        _capi.check(self.lib.cusort_mgpu_wait(self.comm, C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                    "cusort_mgpu_wait")
+
+    @staticmethod
+    def set_timing(enable: bool) -> bool:
+        """Per-phase CUDA-event timing of later sort() calls on this host thread."""
+        return bool(_capi.load().cusort_mgpu_set_timing(int(enable)))
+
+    @staticmethod
+    def phase_times() -> dict:
+        """{phase name: ms} of this thread's last sort() while timing was on."""
+        lib = _capi.load()
+        ms = (C.c_float * 8)()
+        names = (C.c_char_p * 8)()
+        m = lib.cusort_mgpu_get_phase_times(ms, names, 8)
+        return {names[i].decode(): float(ms[i]) for i in range(m)}
+
     def _call(self, temp_ptr, nbytes, kt, vb, kin, vin, n, kout, vout, cap, n_out, b, e, desc):
         stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
         return self.lib.cusort_mgpu_sort(self.comm, temp_ptr, C.byref(nbytes), _capi.key_type_id(kt), vb, kin, vin,
