@@ -61,6 +61,28 @@ __device__ __forceinline__ uint32_t digit_k(U x, U c, U f, uint32_t shift, uint3
   return (uint32_t)(twiddle_k<FLOAT_KEY, U>(x, c, f) >> shift) & mask;
 }
 
+// The same value through an opaque register move: the compiler cannot merge
+// computations on the result with computations on the original (used to keep
+// it from holding derived values live across long stretches of code).
+__device__ __forceinline__ uint8_t opaque(uint8_t x) {
+  uint32_t t = x;
+  asm volatile("mov.b32 %0, %0;" : "+r"(t));
+  return (uint8_t)t;
+}
+__device__ __forceinline__ uint16_t opaque(uint16_t x) {
+  uint32_t t = x;
+  asm volatile("mov.b32 %0, %0;" : "+r"(t));
+  return (uint16_t)t;
+}
+__device__ __forceinline__ uint32_t opaque(uint32_t x) {
+  asm volatile("mov.b32 %0, %0;" : "+r"(x));
+  return x;
+}
+__device__ __forceinline__ unsigned long long opaque(unsigned long long x) {
+  asm volatile("mov.b64 %0, %0;" : "+l"(x));
+  return x;
+}
+
 // Streaming (evict-first) global loads of one element.
 __device__ __forceinline__ uint8_t ld_cs(const uint8_t* p) {
   uint16_t v;

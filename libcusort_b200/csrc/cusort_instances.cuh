@@ -110,7 +110,8 @@ template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG =
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB>;
   using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>;
-  os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
+  if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);
+  else os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;
   os->tile = CFG::TILE;
   os->smem = CFG::SMEM_BYTES;
@@ -119,7 +120,8 @@ inline void fill_onesweep(KernelInfo* os) {
 template <int KB, int VB, bool FK, int KPT>
 inline void fill_onesweep_small(KernelInfo* os) {
   using CFG = OnesweepCfg<KB, VB, unsigned int, CUSORT_OS_THREADS, KPT, CUSORT_OS_MINB, FK>;
-  os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
+  if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);
+  else os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;
   os->tile = CFG::TILE;
   os->smem = CFG::SMEM_BYTES;

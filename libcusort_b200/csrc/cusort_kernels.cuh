@@ -582,6 +582,56 @@ struct WarpCounters<5> : WarpCounters<1> {
   }
 };
 
+// Mode 6: mode 4 with one 32-bit counter per (warp, digit) instead of two
+// 16-bit counters per word: the counting and position atomics add 1 or the
+// group size to the digit's own word, with no shift or mask arithmetic per
+// key, at 1 KB instead of 512 B of counters per warp.
+template <>
+struct WarpCounters<6> {
+  static constexpr int NT = 3;
+  static constexpr size_t MASK_WORDS = 64;
+  static constexpr size_t BYTES_PER_WARP = kRadix * 4 + NT * MASK_WORDS * 4;
+  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
+    uint4* w = reinterpret_cast<uint4*>(tab + (size_t)warp * BYTES_PER_WARP);
+    constexpr int V = (int)(BYTES_PER_WARP / 16);
+#pragma unroll
+    for (int i = 0; i < (V + 31) / 32; ++i)
+      if (i * 32 + (int)lane < V) w[lane + 32 * i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  __device__ __forceinline__ static void count_key(uint8_t* tab, uint32_t warp, uint32_t d) {
+    atomicAdd(reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP) + d, 1u);
+  }
+  template <int S>
+  __device__ __forceinline__ static uint32_t rank_slot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
+                                                       uint32_t lt, uint32_t& prev_word) {
+    uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    uint32_t* cnt = base;
+    uint32_t* msk = base + kRadix;
+    const uint32_t word = (uint32_t)(S % NT) * MASK_WORDS + (d >> 2);
+    atomicOr(msk + word, 1u << lane);
+    const uint32_t pl = dev::match_digit_ballot<2>(d);
+    __syncwarp();
+    const uint32_t ph = msk[word];
+    if (S > 0) msk[prev_word] = 0u;  // previous slot's table: read by all lanes before the barrier above
+    prev_word = word;
+    const uint32_t peers = pl & ph;
+    const uint32_t below = __popc(peers & lt);
+    const uint32_t leader = 31u - __clz(peers);
+    uint32_t old = dev::atom_add_shared_if(lane == leader, cnt + d, below + 1u, 0u);
+    old = __shfl_sync(0xffffffffu, old, leader);
+    return old + below;
+  }
+  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
+    reinterpret_cast<uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = v;
+  }
+};
+
 template <int S, int N, class F>
 __device__ __forceinline__ void static_for(F&& f) {
   if constexpr (S < N) {
@@ -633,8 +683,12 @@ struct RankSlots {
 #ifndef CUSORT_KEYS_RANK_MODE
 #define CUSORT_KEYS_RANK_MODE 4
 #endif
+#ifndef CUSORT_OTHER_RANK_MODE
+#define CUSORT_OTHER_RANK_MODE 4
+#endif
 #define CUSORT_RANK_MODE_OF(KB, VB) \
-  (CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE : (((VB) == 0 && (KB) <= 4) ? CUSORT_KEYS_RANK_MODE : 4))
+  (CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE                   \
+                         : (((VB) == 0 && (KB) <= 4) ? CUSORT_KEYS_RANK_MODE : CUSORT_OTHER_RANK_MODE))
 
 template <int KB_, int VB_, typename Off_, int THREADS_, int KPT_, int MINB_, bool FLOAT_KEY_, bool ROUTED_ = false,
           bool SEG_ = false>
@@ -696,6 +750,20 @@ struct OnesweepCfg {
 #define CUSORT_HOT_SHARE 16
 #endif
   static constexpr bool HOT = CUSORT_HOT_DIGIT && RANK_MODE == 4 && !ROUTED_ && !SEG_;
+  // Pipelined register loads (onesweep_pipe_kernel): the next tile's keys and
+  // values are loaded from global memory straight into registers while the
+  // current tile is scattered out of shared memory; no staging copy.
+#ifndef CUSORT_PIPE
+#define CUSORT_PIPE 0
+#endif
+#ifndef CUSORT_PIPE_MAXKB
+#define CUSORT_PIPE_MAXKB 8
+#endif
+#ifndef CUSORT_PIPE_MINKB
+#define CUSORT_PIPE_MINKB 1
+#endif
+  static constexpr bool PIPE = CUSORT_PIPE && !ROUTED_ && !SEG_ && !VSMEM && !PREFETCH && !HOT &&
+                               RANK_MODE >= 4 && KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB;
   static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
   static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
@@ -1231,6 +1299,225 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
   }
   if constexpr (CFG::ROUTED) __threadfence_system();  // peer stores visible before the kernel ends
+}
+
+// ---------------------------------------------------------------------------
+// onesweep, pipelined register loads (CFG::PIPE; plain passes).  The same
+// stable pass as onesweep_kernel, re-ordered so that no CTA waits for its
+// tile's data:
+//   prologue   ticket t0; issue t0's loads (global -> registers)
+//   per tile   count digits (registers) -> aggregate publish -> block scan ->
+//              lookback + rank/reorder into the shared-memory tile ->
+//              ticket t+1 -> ISSUE t+1's loads into the now free registers ->
+//              scatter tile t from shared memory (the loads land meanwhile)
+// Slots past the end of the last tile hold a sentinel key whose twiddled
+// bits are all ones, so every slot's digit is computed the same way (the
+// sentinels take the top digit and sort behind the tile's valid items, which
+// are the only ones written).  The next ticket is taken once the tile is
+// reordered, so the next tile's aggregate is published about one scatter
+// later -- the same delay as a tile load, which it replaces.
+// ---------------------------------------------------------------------------
+#ifndef CUSORT_PIPE_SCATTER_UNROLL
+#define CUSORT_PIPE_SCATTER_UNROLL 4
+#endif
+// Issues the global loads of tile t for one thread (slot s = item first + 32 s
+// of the tile) into registers; slots past the end get the sentinel key.
+template <class CFG, typename K, typename V, int NV>
+__device__ __forceinline__ void pipe_load_tile(K (&key)[CFG::KPT], V (&val)[NV], const K* keys_in, const V* vals_in,
+                                               uint64_t n, uint32_t t, uint32_t first, K sentinel) {
+  constexpr int KPT = CFG::KPT, TILE = CFG::TILE;
+  const uint64_t base = (uint64_t)t * TILE;
+  const uint32_t valid = (uint32_t)((n - base) < (uint64_t)TILE ? (n - base) : (uint64_t)TILE);
+  const K* kin = keys_in + base + first;
+  const V* vin = vals_in + base + first;
+  if (valid == (uint32_t)TILE) {
+#pragma unroll
+    for (int s = 0; s < KPT; ++s) {
+      key[s] = __ldcs(kin + s * 32);
+      if constexpr (CFG::VB > 0) val[s] = __ldcs(vin + s * 32);
+    }
+  } else {
+#pragma unroll
+    for (int s = 0; s < KPT; ++s) {
+      const bool in = first + s * 32 < valid;
+      key[s] = in ? __ldcs(kin + s * 32) : sentinel;
+      if constexpr (CFG::VB > 0) {
+        if (in) val[s] = __ldcs(vin + s * 32);
+      }
+    }
+  }
+}
+template <class CFG>
+__global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(const OnesweepArgs a) {
+  using K = typename dev::UIntOf<CFG::KB>::T;
+  using V = typename dev::UIntOf<(CFG::VB ? CFG::VB : 1)>::T;
+  using Off = typename CFG::Off;
+  using DB = DescBits<Off>;
+  using WC = typename CFG::WC;
+  constexpr int THREADS = CFG::THREADS, KPT = CFG::KPT, TILE = CFG::TILE, WARPS = CFG::WARPS;
+  constexpr bool HAS_V = CFG::VB > 0;
+  static_assert(CFG::PIPE && CFG::RANK_MODE >= 4, "pipelined pass: early-count rank modes only");
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  K* s_keys = reinterpret_cast<K*>(smem);  // the tile in sorted order
+  V* s_vals = reinterpret_cast<V*>(smem + CFG::KEYS_BYTES);
+  uint2* s_kv = reinterpret_cast<uint2*>(smem);  // PACKED_KV view
+  uint8_t* s_wtab = smem + CFG::OFF_WTAB;
+  uint32_t* s_tstart = reinterpret_cast<uint32_t*>(smem + CFG::OFF_TSTART);
+  Off* s_gbase = reinterpret_cast<Off*>(smem + CFG::OFF_GBASE);
+  Off* s_goff = reinterpret_cast<Off*>(smem + CFG::OFF_GOFF);
+  uint32_t* s_misc = reinterpret_cast<uint32_t*>(smem + CFG::OFF_MISC);  // [0],[1] tickets, [4..11] scan
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const K tc = (K)a.tw_c, tf = (K)a.tw_f;
+  // a key whose twiddled bits are all ones (dev::twiddle): ~c when c's sign
+  // bit is set (the key's own sign bit is then clear), else ~(c ^ f)
+  constexpr int NB = CFG::KB * 8;
+  const K sentinel = ((tc >> (NB - 1)) & 1) ? (K)~tc : (K)~(tc ^ tf);
+  const K* keys_in = static_cast<const K*>(a.keys_in);
+  K* keys_out = static_cast<K*>(a.keys_out);
+  const V* vals_in = static_cast<const V*>(a.vals_in);
+  V* vals_out = static_cast<V*>(a.vals_out);
+  Off* desc = static_cast<Off*>(a.desc);
+  const uint32_t num_tiles = a.num_tiles;
+
+  dev::pdl_wait();
+  dev::pdl_launch_dependents();
+  if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
+  {
+    // global exclusive offset of every digit (upfront histogram)
+    Off cv = (tid < kRadix) ? static_cast<const Off*>(a.g_hist_pass)[tid] : Off(0);
+    Off incl = cv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      Off t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= (uint32_t)o) incl += t;
+    }
+    if (lane == 31 && warp < 8) s_goff[warp] = incl;
+    WC::zero(s_wtab, warp, lane);
+    __syncthreads();
+    if (tid < kRadix) {
+      Off pre = 0;
+      for (uint32_t w = 0; w < warp; ++w) pre += s_goff[w];
+      s_gbase[tid] = pre + incl - cv;
+    }
+  }
+  uint32_t cur = s_misc[0];
+  const uint32_t lt = dev::lanemask_lt();
+  const uint32_t wfirst = warp * (KPT * 32);
+  K key[KPT];
+  V val[HAS_V ? KPT : 1];
+
+  // issue the loads of tile t into key[] / val[] (consumed later)
+  auto load_tile = [&](uint32_t t) {
+    pipe_load_tile<CFG>(key, val, keys_in, vals_in, a.n, t, wfirst + lane, sentinel);
+  };
+  if (cur < num_tiles) load_tile(cur);
+
+  while (cur < num_tiles) {
+    const uint32_t tile = cur;
+    const uint64_t base = (uint64_t)tile * TILE;
+    const uint32_t valid = (uint32_t)((a.n - base) < (uint64_t)TILE ? (a.n - base) : (uint64_t)TILE);
+    const bool publish = (int64_t)tile != a.skip_tile;
+    auto digit = [&](int s) -> uint32_t { return dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask); };
+
+    // ---- counting pre-pass (per-warp digit counts).  The digit is taken from
+    // an opaque copy of the key: otherwise the compiler keeps every slot's
+    // digit live until the ranking recomputes it, and spills registers.
+#pragma unroll
+    for (int s = 0; s < KPT; ++s)
+      WC::count_key(s_wtab, warp, dev::digit_k<CFG::FLOAT_KEY, K>(dev::opaque(key[s]), tc, tf, a.shift, a.mask));
+    __syncthreads();
+
+    // ---- per-digit counts, aggregate publish, tile-local digit offsets
+    uint32_t cnt = 0;
+    if (tid < kRadix) {
+#pragma unroll 4
+      for (int w = 0; w < WARPS; ++w) {
+        const uint32_t c = WC::count(s_wtab, w, tid);
+        WC::put(s_wtab, w, tid, cnt);
+        cnt += c;
+      }
+      if (tid == a.mask) cnt -= (uint32_t)TILE - valid;  // the sentinels
+      if (publish)
+        dev::st_relaxed(desc + (size_t)tile * kRadix + tid,
+                        DB::make(a.pass, tile == 0 ? kDescInclusive : kDescAggregate, (Off)cnt));
+    }
+    uint32_t incl = 0;
+    if (warp < kRadix / 32) {
+      incl = dev::warp_inclusive_scan(cnt, lane);
+      if (lane == 31) s_misc[4 + warp] = incl;
+    }
+    __syncthreads();
+    if (tid < kRadix) {
+      uint32_t pre = 0;
+      for (uint32_t w = 0; w < warp; ++w) pre += s_misc[4 + w];
+      const uint32_t ts = pre + incl - cnt;
+      s_tstart[tid] = ts;
+#pragma unroll 4
+      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
+    }
+    __syncthreads();
+
+    // ---- decoupled lookback (digit-owning warps first), then rank + reorder
+    if (tid < kRadix) {
+      Off excl = 0;
+      if (tile > 0) {
+        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns);
+        if (publish) dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
+      }
+      s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+    }
+    {
+      uint32_t prev = 0;
+      static_for<0, KPT>([&](auto sc) {
+        constexpr int S = decltype(sc)::value;
+        const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, digit(S), lane, lt, prev);
+        if constexpr (CFG::PACKED_KV) {
+          s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
+        } else {
+          s_keys[pos] = key[S];
+          if constexpr (HAS_V) s_vals[pos] = val[S];
+        }
+      });
+    }
+    if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
+    __syncthreads();
+
+    // ---- next tile's loads in flight while this tile is written out
+    const uint32_t nxt = s_misc[1];
+#ifndef EXP_LATE
+    if (nxt < num_tiles) load_tile(nxt);
+#endif
+    WC::zero(s_wtab, warp, lane);  // this warp's table: its ranking is done
+
+    // ---- coalesced scatter
+    auto put_one = [&](uint32_t j) {
+      if constexpr (CFG::PACKED_KV) {
+        const uint2 kv = s_kv[j];
+        const K k = (K)kv.x;
+        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        keys_out[dst] = k;
+        vals_out[dst] = (V)kv.y;
+      } else {
+        const K k = s_keys[j];
+        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        keys_out[dst] = k;
+        if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+      }
+    };
+    if (valid == (uint32_t)TILE) {
+      constexpr int SU = CUSORT_PIPE_SCATTER_UNROLL;
+#pragma unroll SU
+      for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS);
+    } else {
+      for (uint32_t j = tid; j < valid; j += THREADS) put_one(j);
+    }
+#ifdef EXP_LATE
+    if (nxt < num_tiles) load_tile(nxt);
+#endif
+    cur = nxt;
+  }
 }
 
 }  // namespace cusort_b200
