@@ -820,12 +820,14 @@ struct DescBits {
 // predecessors.
 template <typename Off, int W>
 __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, uint32_t digit, uint32_t pass,
-                                               uint32_t* status, uint64_t limit_ns, int64_t floor = 0) {
+                                               uint32_t* status, uint64_t limit_ns, int64_t floor = 0,
+                                               uint32_t* rounds = nullptr) {
   using DB = DescBits<Off>;
   Off excl = 0;
   int64_t j = (int64_t)tile - 1;  // nearest predecessor not yet accounted for
   dev::SpinGuard guard;
   while (j >= floor) {  // floor: first tile of the prefix (a segment's first tile)
+    if (rounds) ++*rounds;
     Off w[W];
 #pragma unroll
     for (int k = 0; k < W; ++k)
@@ -851,6 +853,52 @@ __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, u
   }
   return excl;
 }
+
+// Opt-in lookback timer (compile with CUSORT_LOOKBACK_TIMER=1; plain passes).
+// Per tile, the longest time any digit-owning thread spent in lookback_prefix
+// and its number of descriptor-window rounds are added to three u64 words of
+// the control block: +128 ns, +136 rounds, +144 tiles (zeroed by the init
+// kernel with the rest of the control block, so they cover every pass of one
+// sort).
+#ifndef CUSORT_LOOKBACK_TIMER
+#define CUSORT_LOOKBACK_TIMER 0
+#endif
+constexpr uint32_t kLookbackTimerOffset = 128;
+
+struct LookbackTimer {
+  uint32_t t0 = 0;  // low word of %globaltimer (a lookback takes far less than 4 s)
+  uint32_t r = 0;
+  __device__ __forceinline__ void begin() {
+    if constexpr (CUSORT_LOOKBACK_TIMER) {
+      r = 0;
+      t0 = (uint32_t)dev::globaltimer_ns();
+    }
+  }
+  // digit-owning warps (all lanes) after their lookback: warp maxima into s[0..1]
+  __device__ __forceinline__ void end(uint32_t* s, uint32_t lane) {
+    if constexpr (CUSORT_LOOKBACK_TIMER) {
+      const uint32_t dt = __reduce_max_sync(0xffffffffu, (uint32_t)dev::globaltimer_ns() - t0);
+      const uint32_t rm = __reduce_max_sync(0xffffffffu, r);
+      if (lane == 0) {
+        atomicMax(s, dt);
+        atomicMax(s + 1, rm);
+      }
+    }
+  }
+  // thread 0, after a barrier that follows every end() of the tile: the
+  // tile's maxima into the control block
+  __device__ __forceinline__ void tile_done(uint32_t* s, uint32_t* status) {
+    if constexpr (CUSORT_LOOKBACK_TIMER) {
+      unsigned long long* w = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(status) +
+                                                                    kLookbackTimerOffset);
+      atomicAdd(w, (unsigned long long)s[0]);
+      atomicAdd(w + 1, (unsigned long long)s[1]);
+      atomicAdd(w + 2, 1ull);
+      s[0] = 0;
+      s[1] = 0;
+    }
+  }
+};
 
 template <class CFG>
 __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const typename CFG::Args a) {
@@ -905,6 +953,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 
   // [12..13]: the pass's hot digit, (count << 8 | digit) as u64, 0 if none
   unsigned long long* s_hot = reinterpret_cast<unsigned long long*>(s_misc + 12);
+  constexpr bool TIMED = CUSORT_LOOKBACK_TIMER && !CFG::ROUTED && !CFG::SEG;
+  LookbackTimer lbt;
   if (tid == 0) {
     dev::mbar_init(s_mbar, 1);
     dev::mbar_init(s_mbar + 1, 1);
@@ -912,6 +962,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     s_misc[2] = 0;
     s_misc[3] = 0;
     *s_hot = 0ull;
+    s_misc[14] = 0;  // lookback timer: the tile's maxima
+    s_misc[15] = 0;
   }
   dev::pdl_wait();
   dev::pdl_launch_dependents();
@@ -1198,7 +1250,10 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     if (tid < kRadix) {
       Off excl = 0;
       if (tile > floor) {
-        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, floor);
+        if constexpr (TIMED) lbt.begin();
+        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, floor,
+                                                            TIMED ? &lbt.r : nullptr);
+        if constexpr (TIMED) lbt.end(s_misc + 14, lane);
         if (publish)
           dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
       }
@@ -1216,6 +1271,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
     reorder();
     __syncthreads();
+    if constexpr (TIMED) {
+      if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
+    }
     if constexpr (CFG::ROUTED) {
       // Owner q receives, per source rank, that rank's tiles in order, each
       // tile's items of q in the tile's (digit-sorted) order: one contiguous
@@ -1381,9 +1439,14 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
   Off* desc = static_cast<Off*>(a.desc);
   const uint32_t num_tiles = a.num_tiles;
 
+  LookbackTimer lbt;
   dev::pdl_wait();
   dev::pdl_launch_dependents();
-  if (tid == 0) s_misc[0] = atomicAdd(a.tile_counter, 1u);
+  if (tid == 0) {
+    s_misc[0] = atomicAdd(a.tile_counter, 1u);
+    s_misc[14] = 0;  // lookback timer: the tile's maxima
+    s_misc[15] = 0;
+  }
   {
     // global exclusive offset of every digit (upfront histogram)
     Off cv = (tid < kRadix) ? static_cast<const Off*>(a.g_hist_pass)[tid] : Off(0);
@@ -1463,7 +1526,10 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     if (tid < kRadix) {
       Off excl = 0;
       if (tile > 0) {
-        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns);
+        lbt.begin();
+        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, 0,
+                                                            CUSORT_LOOKBACK_TIMER ? &lbt.r : nullptr);
+        lbt.end(s_misc + 14, lane);
         if (publish) dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
       }
       s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
@@ -1483,12 +1549,11 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     }
     if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
     __syncthreads();
+    if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
 
     // ---- next tile's loads in flight while this tile is written out
     const uint32_t nxt = s_misc[1];
-#ifndef EXP_LATE
     if (nxt < num_tiles) load_tile(nxt);
-#endif
     WC::zero(s_wtab, warp, lane);  // this warp's table: its ranking is done
 
     // ---- coalesced scatter
@@ -1513,9 +1578,6 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     } else {
       for (uint32_t j = tid; j < valid; j += THREADS) put_one(j);
     }
-#ifdef EXP_LATE
-    if (nxt < num_tiles) load_tile(nxt);
-#endif
     cur = nxt;
   }
 }
