@@ -24,11 +24,16 @@ namespace cusort_b200 {
 // Items per thread (KPT) by bytes per item; overridable for tuning.  Larger
 // tiles amortise the per-tile work (column scan, block scan, lookback,
 // ticket) over more keys; the limit is 64 registers per thread at two 512-
-// thread CTAs per SM.  Measured on B200 at 2^26 items: u32 keys-only 36
-// (pass 0.302 -> 0.251 ms from 16 to 32; whole sort 1.045 -> 1.026 ms from 32
-// to 36, 40 and 44 slower), int32/uint32 pairs 20 (0.369 -> 0.356 ms vs 16).
+// thread CTAs per SM.  Measured on B200 at 2^26 items (onesweep launch, 32-bit
+// counters, pipelined loads for 4-byte keys): keys-only 32 (230 us; 28: 235,
+// 36: 243, 40: 246 with spills); 4-byte keys with 4-byte values 16 (341 us;
+// 12: 356, 14: 345, 18: 366, 20: 367 with spills).  The staged kernel of the
+// other widths was tuned at 20 items per thread for pairs of up to 8 bytes.
 #ifndef CUSORT_OS_KPT_KEYS4
-#define CUSORT_OS_KPT_KEYS4 36
+#define CUSORT_OS_KPT_KEYS4 32
+#endif
+#ifndef CUSORT_OS_KPT_K4V4
+#define CUSORT_OS_KPT_K4V4 16
 #endif
 #ifndef CUSORT_OS_KPT_LE8
 #define CUSORT_OS_KPT_LE8 20
@@ -97,6 +102,7 @@ struct TileShape {
                              : (KB == 8 && VB == 16)  ? CUSORT_OS_KPT_K8V16
                              : (KB == 8 && VB == 8) ? CUSORT_OS_KPT_K8V8
                              : (VB == 0 && KB <= 4) ? CUSORT_OS_KPT_KEYS4
+                             : (KB == 4 && VB == 4) ? CUSORT_OS_KPT_K4V4
                              : (BYTES > 16)         ? CUSORT_OS_KPT_GT16
                              : (BYTES > 8)          ? CUSORT_OS_KPT_LE16
                                                     : CUSORT_OS_KPT_LE8;

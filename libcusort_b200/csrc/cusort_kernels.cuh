@@ -582,15 +582,19 @@ struct WarpCounters<5> : WarpCounters<1> {
   }
 };
 
-// Mode 6: mode 4 with one 32-bit counter per (warp, digit) instead of two
-// 16-bit counters per word: the counting and position atomics add 1 or the
-// group size to the digit's own word, with no shift or mask arithmetic per
-// key, at 1 KB instead of 512 B of counters per warp.
-template <>
-struct WarpCounters<6> {
+// Modes 6-8: mode 4 with one 32-bit counter per (warp, digit) instead of
+// two 16-bit counters per word: the counting and position atomics add 1 or
+// the group size to the digit's own word (no shift or mask arithmetic per
+// key, and two different digits never share an atomic's address), at 1 KB
+// instead of 512 B of counters per warp.  BB of the digit's bits are matched
+// by ballot and the other 8 - BB by the shared-memory table of 2^(8-BB)
+// words (mode 6: BB = 2, mode 7: BB = 1, mode 8: BB = 3).
+template <int BB>
+struct WarpCounters32 {
   static constexpr int NT = 3;
-  static constexpr size_t MASK_WORDS = 64;
+  static constexpr size_t MASK_WORDS = (size_t)kRadix >> BB;
   static constexpr size_t BYTES_PER_WARP = kRadix * 4 + NT * MASK_WORDS * 4;
+  static_assert(BYTES_PER_WARP % 16 == 0, "16-byte zeroing");
   __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
     uint4* w = reinterpret_cast<uint4*>(tab + (size_t)warp * BYTES_PER_WARP);
     constexpr int V = (int)(BYTES_PER_WARP / 16);
@@ -607,9 +611,9 @@ struct WarpCounters<6> {
     uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
     uint32_t* cnt = base;
     uint32_t* msk = base + kRadix;
-    const uint32_t word = (uint32_t)(S % NT) * MASK_WORDS + (d >> 2);
+    const uint32_t word = (uint32_t)(S % NT) * MASK_WORDS + (d >> BB);
     atomicOr(msk + word, 1u << lane);
-    const uint32_t pl = dev::match_digit_ballot<2>(d);
+    const uint32_t pl = dev::match_digit_ballot<BB>(d);
     __syncwarp();
     const uint32_t ph = msk[word];
     if (S > 0) msk[prev_word] = 0u;  // previous slot's table: read by all lanes before the barrier above
@@ -631,6 +635,12 @@ struct WarpCounters<6> {
     reinterpret_cast<uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = v;
   }
 };
+template <>
+struct WarpCounters<6> : WarpCounters32<2> {};
+template <>
+struct WarpCounters<7> : WarpCounters32<1> {};
+template <>
+struct WarpCounters<8> : WarpCounters32<3> {};
 
 template <int S, int N, class F>
 __device__ __forceinline__ void static_for(F&& f) {
@@ -681,10 +691,10 @@ struct RankSlots {
 
 // Rank mode per key/value width (measured on B200, see OnesweepCfg).
 #ifndef CUSORT_KEYS_RANK_MODE
-#define CUSORT_KEYS_RANK_MODE 4
+#define CUSORT_KEYS_RANK_MODE 6
 #endif
 #ifndef CUSORT_OTHER_RANK_MODE
-#define CUSORT_OTHER_RANK_MODE 4
+#define CUSORT_OTHER_RANK_MODE 6
 #endif
 #define CUSORT_RANK_MODE_OF(KB, VB) \
   (CUSORT_RANK_MODE >= 0 ? CUSORT_RANK_MODE                   \
@@ -702,10 +712,6 @@ struct OnesweepCfg {
   static constexpr bool SEG = SEG_;
   static_assert(!(ROUTED && SEG), "one special mode at a time");
   using Args = typename std::conditional<SEG, SegOnesweepArgs, OnesweepArgs>::type;
-  // Measured on B200 (2^26 items): mode 4 is fastest for pairs and 8-byte
-  // keys; for keys-only <= 4 bytes its extra registers spill and mode 3 wins.
-  static constexpr int RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
-  using WC = WarpCounters<RANK_MODE>;
   using Off = Off_;
   static constexpr int WARPS = THREADS / 32;
   static constexpr int TILE = THREADS * KPT;
@@ -714,8 +720,6 @@ struct OnesweepCfg {
   // while the current one is processed.
   static constexpr size_t KEYS_BYTES = align_up((size_t)TILE * KB, 128);
   static constexpr size_t BUF_BYTES = KEYS_BYTES + align_up((size_t)TILE * VB, 128);
-  static constexpr size_t REST_BYTES = align_up((size_t)WARPS * WC::BYTES_PER_WARP, 16) + kRadix * 4 +
-                                       2 * kRadix * sizeof(Off) + 16 * 4 + 32;
   static constexpr size_t SMEM_PER_CTA = (227 * 1024) / MINB - 1024;
   static constexpr bool PREFETCH = CUSORT_PREFETCH != 0;
   static constexpr bool DIRECT_LOAD = CUSORT_DIRECT_LOAD >= 0 ? (CUSORT_DIRECT_LOAD == 1) : (VB_ == 0 && KB_ <= 4);
@@ -732,6 +736,27 @@ struct OnesweepCfg {
 #define CUSORT_VSMEM_MAXKB 4
 #endif
   static constexpr bool VSMEM = CUSORT_VSMEM && VB_ > 0 && VB_ <= 2 && KB_ <= CUSORT_VSMEM_MAXKB;
+  // Routed passes' tables (layout below).
+  static constexpr size_t ROUTE_LAYOUT_BYTES =
+      ROUTED ? (kRadix + 4 * 8 * kMaxRouteRanks + 8 * (kRadix + 8) + 2 * 4 * kMaxRouteRanks + 2 * 8 * kRadix) : 0;
+  // Everything but the per-warp tables (one staging buffer).
+  static constexpr size_t NON_WTAB_BYTES = BUF_BYTES + 16 + kRadix * 4 + 2 * kRadix * sizeof(Off) + 16 * 4 + 32 +
+                                           (VSMEM ? align_up((size_t)TILE * VB, 16) : 0) + ROUTE_LAYOUT_BYTES;
+  // Rank mode (WarpCounters): the preferred one for the key/value width --
+  // measured on B200 at 2^26 items, the 32-bit counters of mode 6 beat the
+  // packed 16-bit counters of mode 4 for every 4-byte-key shape (2-5 % on
+  // uniform keys, 18-26 % on skewed ones) -- unless its larger tables would
+  // push the CTA past its share of shared memory (MINB CTAs per SM), where
+  // mode 4 keeps the tile shape's occupancy.
+  static constexpr int PREF_RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
+  static constexpr int RANK_MODE =
+      (PREF_RANK_MODE >= 6 && NON_WTAB_BYTES + (size_t)WARPS * WarpCounters<(PREF_RANK_MODE >= 6 ? PREF_RANK_MODE : 6)>::BYTES_PER_WARP >
+                                  SMEM_PER_CTA)
+          ? 4
+          : PREF_RANK_MODE;
+  using WC = WarpCounters<RANK_MODE>;
+  static constexpr size_t REST_BYTES = align_up((size_t)WARPS * WC::BYTES_PER_WARP, 16) + kRadix * 4 +
+                                       2 * kRadix * sizeof(Off) + 16 * 4 + 32;
   // Mode 4 needs a key's digit twice (count, rank); recomputing it from the
   // key instead of keeping a digit array frees KPT registers, which buys
   // larger tiles (2 = every width, 1 = keys-only, 0 = never).
@@ -739,7 +764,7 @@ struct OnesweepCfg {
 #define CUSORT_RECOMPUTE_DIGIT 2
 #endif
   static constexpr bool RECOMPUTE_DIGIT =
-      CUSORT_RANK_MODE_OF(KB_, VB_) >= 4 && (CUSORT_RECOMPUTE_DIGIT == 2 || (CUSORT_RECOMPUTE_DIGIT == 1 && VB_ == 0));
+      RANK_MODE >= 4 && (CUSORT_RECOMPUTE_DIGIT == 2 || (CUSORT_RECOMPUTE_DIGIT == 1 && VB_ == 0));
   // Hot-digit ranking (WarpCounters<4>::count_key_hot / rank_slot_hot) when
   // a digit holds more than 1/CUSORT_HOT_SHARE of the pass's items; plain
   // passes only (the counts come from the upfront histogram).
@@ -753,17 +778,36 @@ struct OnesweepCfg {
   // Pipelined register loads (onesweep_pipe_kernel): the next tile's keys and
   // values are loaded from global memory straight into registers while the
   // current tile is scattered out of shared memory; no staging copy.
+// Measured on B200 at 2^26 items (onesweep launch, 32-bit counters): 4-byte
+// keys-only 239 -> 230 us, int32 + uint32 pairs 342 -> 341 us (at 32 and 16
+// items per thread), float keys 259 -> 240 us; the next tile's aggregate is
+// published later, which the lookback timer sees (about 4 descriptor-window
+// rounds per tile instead of 3.6).  Other key widths keep the staged kernel.
 #ifndef CUSORT_PIPE
-#define CUSORT_PIPE 0
+#define CUSORT_PIPE 1
 #endif
 #ifndef CUSORT_PIPE_MAXKB
-#define CUSORT_PIPE_MAXKB 8
+#define CUSORT_PIPE_MAXKB 4
 #endif
 #ifndef CUSORT_PIPE_MINKB
-#define CUSORT_PIPE_MINKB 1
+#define CUSORT_PIPE_MINKB 4
 #endif
+#ifndef CUSORT_PIPE_MAXVB
+#define CUSORT_PIPE_MAXVB 4
+#endif
+  // Integer keys of plain passes: the twiddle of the pass's digit is a
+  // constant xor, a bijection on digits.  The per-warp tables, the ranking and
+  // the digit offsets used by the scatter are then indexed by the raw digit
+  // (key >> shift) & mask, and the xor moves into the per-tile scan (digit t's
+  // entries sit at t ^ (twiddle constant's digit)): one instruction less per
+  // digit computation, three per key.
+#ifndef CUSORT_FOLD_TWIDDLE
+#define CUSORT_FOLD_TWIDDLE 0
+#endif
+  static constexpr bool FOLD = CUSORT_FOLD_TWIDDLE && !FLOAT_KEY_ && !ROUTED_ && !SEG_;
   static constexpr bool PIPE = CUSORT_PIPE && !ROUTED_ && !SEG_ && !VSMEM && !PREFETCH && !HOT &&
-                               RANK_MODE >= 4 && KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB;
+                               RANK_MODE >= 4 && KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB &&
+                               VB_ <= CUSORT_PIPE_MAXVB;
   static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
   static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
@@ -783,6 +827,7 @@ struct OnesweepCfg {
   static constexpr size_t OFF_RFIRST = OFF_RPRE + 8 * (kRadix + 8);
   static constexpr size_t OFF_RDST = OFF_RFIRST + 2 * 4 * kMaxRouteRanks;
   static constexpr size_t ROUTE_BYTES = ROUTED ? (OFF_RDST + 2 * 8 * kRadix - OFF_ROUTE) : 0;
+  static_assert(ROUTE_BYTES == ROUTE_LAYOUT_BYTES, "routed table layout");
   static_assert(!(ROUTED && PREFETCH), "routed passes take tickets one tile at a time");
   static constexpr size_t SMEM_BYTES = OFF_ROUTE + ROUTE_BYTES;
   static_assert(THREADS >= kRadix && THREADS % 32 == 0, "need >= 256 threads");
@@ -793,9 +838,12 @@ struct OnesweepCfg {
 
 // Predecessor words read per lookback round trip: 8 with 32-bit words; 4 with
 // 64-bit words (n >= 2^30), where 8 would make the pass spill registers.
+#ifndef CUSORT_LOOKBACK_WINDOW
+#define CUSORT_LOOKBACK_WINDOW 8
+#endif
 template <typename Off>
 constexpr int lookback_window() {
-  return sizeof(Off) == 8 ? 4 : 8;
+  return sizeof(Off) == 8 ? CUSORT_LOOKBACK_WINDOW / 2 : CUSORT_LOOKBACK_WINDOW;
 }
 
 template <typename Off>
@@ -821,7 +869,7 @@ struct DescBits {
 template <typename Off, int W>
 __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, uint32_t digit, uint32_t pass,
                                                uint32_t* status, uint64_t limit_ns, int64_t floor = 0,
-                                               uint32_t* rounds = nullptr) {
+                                               uint32_t* rounds = nullptr, uint32_t* empties = nullptr) {
   using DB = DescBits<Off>;
   Off excl = 0;
   int64_t j = (int64_t)tile - 1;  // nearest predecessor not yet accounted for
@@ -846,6 +894,7 @@ __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, u
     }
     if (done) break;
     j -= consumed;
+    if (empties && consumed == 0) ++*empties;
     if (consumed == 0 && guard.expired(status, limit_ns)) {
       atomicOr(status, kStatusLookbackTimeout);
       break;
@@ -855,11 +904,12 @@ __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, u
 }
 
 // Opt-in lookback timer (compile with CUSORT_LOOKBACK_TIMER=1; plain passes).
-// Per tile, the longest time any digit-owning thread spent in lookback_prefix
-// and its number of descriptor-window rounds are added to three u64 words of
-// the control block: +128 ns, +136 rounds, +144 tiles (zeroed by the init
-// kernel with the rest of the control block, so they cover every pass of one
-// sort).
+// Adds to u64 words of the control block (zeroed by the init kernel with the
+// rest of it, so they cover every pass of one sort): +128 the sum over tiles
+// of the longest time any digit-owning thread of the tile spent in
+// lookback_prefix (ns), +136 descriptor-window rounds summed over all digit
+// threads and tiles, +144 tiles, +152 the rounds among those that re-polled
+// because the nearest unaccounted predecessor had published nothing yet.
 #ifndef CUSORT_LOOKBACK_TIMER
 #define CUSORT_LOOKBACK_TIMER 0
 #endif
@@ -867,35 +917,37 @@ constexpr uint32_t kLookbackTimerOffset = 128;
 
 struct LookbackTimer {
   uint32_t t0 = 0;  // low word of %globaltimer (a lookback takes far less than 4 s)
-  uint32_t r = 0;
+  uint32_t r = 0, e = 0;
   __device__ __forceinline__ void begin() {
     if constexpr (CUSORT_LOOKBACK_TIMER) {
       r = 0;
+      e = 0;
       t0 = (uint32_t)dev::globaltimer_ns();
     }
   }
-  // digit-owning warps (all lanes) after their lookback: warp maxima into s[0..1]
-  __device__ __forceinline__ void end(uint32_t* s, uint32_t lane) {
+  // digit-owning warps (all lanes) after their lookback
+  __device__ __forceinline__ void end(uint32_t* s, uint32_t lane, uint32_t* status) {
     if constexpr (CUSORT_LOOKBACK_TIMER) {
       const uint32_t dt = __reduce_max_sync(0xffffffffu, (uint32_t)dev::globaltimer_ns() - t0);
-      const uint32_t rm = __reduce_max_sync(0xffffffffu, r);
+      const uint32_t rs = __reduce_add_sync(0xffffffffu, r);
+      const uint32_t es = __reduce_add_sync(0xffffffffu, e);
       if (lane == 0) {
         atomicMax(s, dt);
-        atomicMax(s + 1, rm);
+        unsigned long long* w = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(status) +
+                                                                      kLookbackTimerOffset);
+        atomicAdd(w + 1, (unsigned long long)rs);
+        atomicAdd(w + 3, (unsigned long long)es);
       }
     }
   }
-  // thread 0, after a barrier that follows every end() of the tile: the
-  // tile's maxima into the control block
+  // thread 0, after a barrier that follows every end() of the tile
   __device__ __forceinline__ void tile_done(uint32_t* s, uint32_t* status) {
     if constexpr (CUSORT_LOOKBACK_TIMER) {
       unsigned long long* w = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(status) +
                                                                     kLookbackTimerOffset);
       atomicAdd(w, (unsigned long long)s[0]);
-      atomicAdd(w + 1, (unsigned long long)s[1]);
       atomicAdd(w + 2, 1ull);
       s[0] = 0;
-      s[1] = 0;
     }
   }
 };
@@ -930,6 +982,13 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   uint32_t num_tiles = a.num_tiles;  // segmented: the planner's count, read after the PDL wait
   const bool tma_ok = a.tma_keys && (!HAS_V || a.tma_vals);
   const uint64_t pol = dev::l2_policy_evict_first();
+  // digit of a key as the tables index it (the raw digit when CFG::FOLD; cx
+  // maps a digit to its table index and back)
+  const uint32_t cx = CFG::FOLD ? (uint32_t)((unsigned long long)tc >> a.shift) & a.mask : 0u;
+  auto kdigit = [&](K k) -> uint32_t {
+    if constexpr (CFG::FOLD) return (uint32_t)(k >> a.shift) & a.mask;
+    else return dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
+  };
 
   // A tile is staged by TMA when it is full and both inputs are 16-byte aligned.
   auto tma_tile = [&](uint32_t t) {
@@ -1118,7 +1177,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     // digit of slot s (the top digit for slots past the end of the tile)
     auto digit_at = [&](int s) -> uint32_t {
       const uint32_t idx = wfirst_c + s * 32 + lane;
-      return (idx < valid) ? dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask) : a.mask;
+      return (idx < valid) ? kdigit(key[s]) : (a.mask ^ cx);
     };
     V val[VREG ? KPT : 1];
     const uint32_t wfirst = wfirst_c;
@@ -1157,7 +1216,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
     constexpr bool EARLY = CFG::RANK_MODE >= 4;
     // the pass's hot digit (256: none); written before the first tile's barrier
-    const uint32_t hot = (CFG::HOT && *s_hot != 0ull) ? (uint32_t)(*s_hot & 0xffu) : 256u;
+    const uint32_t hot = (CFG::HOT && *s_hot != 0ull) ? ((uint32_t)(*s_hot & 0xffu) ^ cx) : 256u;
     if constexpr (EARLY) {
       if (__builtin_expect(!CFG::HOT || hot >= 256u, 1)) {
 #pragma unroll
@@ -1178,8 +1237,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     if (tid < kRadix) {
 #pragma unroll 4
       for (int w = 0; w < WARPS; ++w) {
-        const uint32_t c = WC::count(s_wtab, w, tid);
-        WC::put(s_wtab, w, tid, cnt);
+        const uint32_t c = WC::count(s_wtab, w, tid ^ cx);
+        WC::put(s_wtab, w, tid ^ cx, cnt);
         cnt += c;
       }
       if (tid == a.mask) cnt -= (uint32_t)TILE - valid;
@@ -1199,7 +1258,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       const uint32_t ts = pre + incl - cnt;
       s_tstart[tid] = ts;
 #pragma unroll 4
-      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
+      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid ^ cx, WC::get(s_wtab, w, tid ^ cx) + ts);
     }
     __syncthreads();
 
@@ -1252,8 +1311,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       if (tile > floor) {
         if constexpr (TIMED) lbt.begin();
         excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, floor,
-                                                            TIMED ? &lbt.r : nullptr);
-        if constexpr (TIMED) lbt.end(s_misc + 14, lane);
+                                                            TIMED ? &lbt.r : nullptr, TIMED ? &lbt.e : nullptr);
+        if constexpr (TIMED) lbt.end(s_misc + 14, lane, a.status);
         if (publish)
           dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
       }
@@ -1266,7 +1325,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         s_pre[tid] = incl_x;
         if (lane == 31) s_pre[kRadix + warp] = incl_x;
       } else {
-        s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+        s_goff[tid ^ cx] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
     }
     reorder();
@@ -1334,12 +1393,12 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       } else if constexpr (CFG::PACKED_KV) {
         const uint2 kv = s_kv[j];
         const K k = (K)kv.x;
-        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
         vals_out[dst] = (V)kv.y;
       } else {
         const K k = s_keys[j];
-        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
         if constexpr (HAS_V) vals_out[dst] = s_vsort[j];
       }
@@ -1377,6 +1436,12 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 // ---------------------------------------------------------------------------
 #ifndef CUSORT_PIPE_SCATTER_UNROLL
 #define CUSORT_PIPE_SCATTER_UNROLL 4
+#endif
+#ifndef CUSORT_LOOKBACK_LATE
+#define CUSORT_LOOKBACK_LATE 0
+#endif
+#ifndef CUSORT_LOOKBACK_LATE_WINDOW
+#define CUSORT_LOOKBACK_LATE_WINDOW 16
 #endif
 // Issues the global loads of tile t for one thread (slot s = item first + 32 s
 // of the tile) into registers; slots past the end get the sentinel key.
@@ -1432,6 +1497,11 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
   // bit is set (the key's own sign bit is then clear), else ~(c ^ f)
   constexpr int NB = CFG::KB * 8;
   const K sentinel = ((tc >> (NB - 1)) & 1) ? (K)~tc : (K)~(tc ^ tf);
+  const uint32_t cx = CFG::FOLD ? (uint32_t)((unsigned long long)tc >> a.shift) & a.mask : 0u;
+  auto kdigit = [&](K k) -> uint32_t {
+    if constexpr (CFG::FOLD) return (uint32_t)(k >> a.shift) & a.mask;
+    else return dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
+  };
   const K* keys_in = static_cast<const K*>(a.keys_in);
   K* keys_out = static_cast<K*>(a.keys_out);
   const V* vals_in = static_cast<const V*>(a.vals_in);
@@ -1482,14 +1552,14 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     const uint64_t base = (uint64_t)tile * TILE;
     const uint32_t valid = (uint32_t)((a.n - base) < (uint64_t)TILE ? (a.n - base) : (uint64_t)TILE);
     const bool publish = (int64_t)tile != a.skip_tile;
-    auto digit = [&](int s) -> uint32_t { return dev::digit_k<CFG::FLOAT_KEY, K>(key[s], tc, tf, a.shift, a.mask); };
+    auto digit = [&](int s) -> uint32_t { return kdigit(key[s]); };
 
     // ---- counting pre-pass (per-warp digit counts).  The digit is taken from
     // an opaque copy of the key: otherwise the compiler keeps every slot's
     // digit live until the ranking recomputes it, and spills registers.
 #pragma unroll
     for (int s = 0; s < KPT; ++s)
-      WC::count_key(s_wtab, warp, dev::digit_k<CFG::FLOAT_KEY, K>(dev::opaque(key[s]), tc, tf, a.shift, a.mask));
+      WC::count_key(s_wtab, warp, kdigit(dev::opaque(key[s])));
     __syncthreads();
 
     // ---- per-digit counts, aggregate publish, tile-local digit offsets
@@ -1497,8 +1567,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     if (tid < kRadix) {
 #pragma unroll 4
       for (int w = 0; w < WARPS; ++w) {
-        const uint32_t c = WC::count(s_wtab, w, tid);
-        WC::put(s_wtab, w, tid, cnt);
+        const uint32_t c = WC::count(s_wtab, w, tid ^ cx);
+        WC::put(s_wtab, w, tid ^ cx, cnt);
         cnt += c;
       }
       if (tid == a.mask) cnt -= (uint32_t)TILE - valid;  // the sentinels
@@ -1518,22 +1588,33 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
       const uint32_t ts = pre + incl - cnt;
       s_tstart[tid] = ts;
 #pragma unroll 4
-      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
+      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid ^ cx, WC::get(s_wtab, w, tid ^ cx) + ts);
     }
     __syncthreads();
 
-    // ---- decoupled lookback (digit-owning warps first), then rank + reorder
-    if (tid < kRadix) {
-      Off excl = 0;
-      if (tile > 0) {
-        lbt.begin();
-        excl = lookback_prefix<Off, lookback_window<Off>()>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, 0,
-                                                            CUSORT_LOOKBACK_TIMER ? &lbt.r : nullptr);
-        lbt.end(s_misc + 14, lane);
-        if (publish) dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
+    // ---- decoupled lookback and rank + reorder.  CUSORT_LOOKBACK_LATE = 0:
+    // the digit-owning warps look back first (their L2 round trips overlap
+    // the other warps' reordering) with a window small enough to fit beside
+    // the tile's keys in registers; 1: after their own reordering, when the
+    // keys' registers are free, with a window of CUSORT_LOOKBACK_LATE_WINDOW
+    // predecessors, so that one round usually reaches an inclusive word.
+    auto lookback = [&](auto window_tag) {
+      constexpr int W = decltype(window_tag)::value;
+      if (tid < kRadix) {
+        Off excl = 0;
+        if (tile > 0) {
+          lbt.begin();
+          excl = lookback_prefix<Off, W>(desc, tile, tid, a.pass, a.status, a.spin_limit_ns, 0,
+                                         CUSORT_LOOKBACK_TIMER ? &lbt.r : nullptr,
+                                         CUSORT_LOOKBACK_TIMER ? &lbt.e : nullptr);
+          lbt.end(s_misc + 14, lane, a.status);
+          if (publish)
+            dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
+        }
+        s_goff[tid ^ cx] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
-      s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
-    }
+    };
+    if constexpr (!CUSORT_LOOKBACK_LATE) lookback(std::integral_constant<int, lookback_window<Off>()>{});
     {
       uint32_t prev = 0;
       static_for<0, KPT>([&](auto sc) {
@@ -1547,6 +1628,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
         }
       });
     }
+    if constexpr (CUSORT_LOOKBACK_LATE)
+      lookback(std::integral_constant<int, sizeof(Off) == 8 ? CUSORT_LOOKBACK_LATE_WINDOW / 2
+                                                            : CUSORT_LOOKBACK_LATE_WINDOW>{});
     if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
     __syncthreads();
     if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
@@ -1561,12 +1645,12 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
       if constexpr (CFG::PACKED_KV) {
         const uint2 kv = s_kv[j];
         const K k = (K)kv.x;
-        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
         vals_out[dst] = (V)kv.y;
       } else {
         const K k = s_keys[j];
-        const Off dst = s_goff[dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask)] + (Off)j;
+        const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
         if constexpr (HAS_V) vals_out[dst] = s_vals[j];
       }

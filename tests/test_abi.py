@@ -131,7 +131,7 @@ def _tile_items(kt, vb, n):
 
 
 @pytest.mark.parametrize("kt", [4, 5, 8])  # u32, i32, f32
-@pytest.mark.parametrize("vb,big", [(0, 512 * 36), (4, 512 * 20)])
+@pytest.mark.parametrize("vb,big", [(0, 512 * 32), (4, 512 * 16)])
 def test_tile_tiers(kt, vb, big):
     # 4-byte keys, keys-only or 4-byte values: 8 items per thread up to 2^20 items, 16 up to
     # 2^23, the large tile above (so a small sort's grid still covers the SMs)
