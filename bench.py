@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--profile-case", choices=["u32_keys", "i32_u32_pairs", "i32_u32_pairs_lowent", "u16_keys",
                                                "seg_i32_u32_pairs_1000"], default=None,
                     help="only run --warmup + --steps sorts of this case (for ncu captures)")
+    ap.add_argument("--lookback-stall", action="store_true",
+                    help="report the lookback timer of a library built with CUSORT_LOOKBACK_TIMER=1 (see build.py)")
     return ap.parse_args()
 
 
@@ -707,6 +709,45 @@ def profile_case(args, torch):
     print(json.dumps({"profile_case": args.profile_case, "n": n, "impl": args.impl, "sorts": args.warmup + args.steps}))
 
 
+def lookback_stall(args, torch):
+    """Share of the onesweep time spent in the decoupled lookback, from a library built with
+    CUSORT_NVCC_DEFINES=-DCUSORT_LOOKBACK_TIMER=1: after one sort the control block holds, summed
+    over every tile of every pass, the longest time any digit-owning thread of the tile spent in
+    the lookback (ns), the descriptor-window rounds of all digit threads, the tile count and the
+    rounds that re-polled a predecessor with nothing published.  frac = that time / (onesweep
+    CTAs x the passes' summed launch time): the share of each CTA's time its digit-owning warps
+    were held by the lookback (the other warps reorder meanwhile)."""
+    device = torch.device("cuda", 0)
+    n = 1 << args.log2n
+    out = {"lookback_stall": True, "n": n}
+    from libcusort_b200 import _capi
+    lib = _capi.load()
+    for name, kt, kid, vb in (("i32_u32_pairs", "i32", 5, 4), ("u32_keys", "u32", 4, 0)):
+        keys, vals = make_inputs(torch, n, seed=2, device=device)
+        kin, vin = keys.view(torch.uint8), vals.view(torch.uint8)
+        kout, vout = torch.empty_like(kin), torch.empty_like(vin)
+        s = Sorter("ours", torch, kt, kid, 4, vb, n, kin, kout, vin, vout, torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            s()
+        lib.cusort_set_kernel_timing(1)
+        s()
+        buf, kinds = (C.c_float * 16)(), (C.c_int * 16)()
+        m = lib.cusort_get_kernel_times(buf, kinds, 16)
+        lib.cusort_set_kernel_timing(0)
+        os_ms = sum(buf[i] for i in range(m) if kinds[i] == 2)
+        torch.cuda.synchronize()
+        w = s.temp[128:160].view(torch.int64).tolist()
+        if w[2] == 0:
+            out[name] = {"error": "no timer words: the library was not built with CUSORT_LOOKBACK_TIMER=1"}
+            continue
+        grid = C.c_int(0)
+        lib.cusort_query_plan(kid, vb, n, 0, 32, None, None, C.byref(grid), None, None)
+        out[name] = {"onesweep_ms_4_passes": os_ms, "ctas": grid.value, "tiles": w[2],
+                     "lookback_ns_per_tile": w[0] / w[2], "frac": w[0] / grid.value / (os_ms * 1e6),
+                     "rounds_per_digit_tile": w[1] / w[2] / 256, "empty_round_share": w[3] / max(w[1], 1)}
+    print(json.dumps(out))
+
+
 def main():
     args = parse()
     import torch
@@ -728,6 +769,9 @@ def main():
                                                                   "(needs the reference checkout at build time)"}))
             return
     torch.cuda.set_device(0)
+    if args.lookback_stall:
+        lookback_stall(args, torch)
+        return
     if args.profile_case:
         profile_case(args, torch)
         return

@@ -4,6 +4,11 @@ Every .cu under csrc/ is compiled for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a) in parallel, then linked into one
 shared library with the CUDA runtime linked statically and NCCL dynamically.
 Run as ``python -m libcusort_b200.build`` or through ``__graft_entry__.build()``.
+
+Environment CUSORT_NVCC_DEFINES adds preprocessor definitions to every
+compile (e.g. ``-DCUSORT_LOOKBACK_TIMER=1`` for the lookback-timer build that
+``bench.py --lookback-stall`` reads); the definitions of the last build are
+kept beside the library, so a change of them forces a rebuild.
 """
 from __future__ import annotations
 
@@ -23,6 +28,16 @@ LIB = OUT_DIR / "libcusort_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr"]
+STAMP = OUT_DIR / "defines.txt"
+
+
+def extra_defines() -> list[str]:
+    """-D flags from CUSORT_NVCC_DEFINES (anything else there is rejected)."""
+    flags = os.environ.get("CUSORT_NVCC_DEFINES", "").split()
+    bad = [f for f in flags if not f.startswith("-D")]
+    if bad:
+        raise ValueError(f"CUSORT_NVCC_DEFINES takes -D flags only, got {bad}")
+    return flags
 
 
 def nvcc() -> str:
@@ -42,7 +57,8 @@ def nccl_flags() -> list[str]:
 
 def _compile(src: Path, verbose: bool) -> tuple[Path, str]:
     obj = OBJ_DIR / (src.stem + ".o")
-    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *nccl_flags(), "-Xptxas", "-v", "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *extra_defines(), *nccl_flags(), "-Xptxas", "-v", "-c", str(src), "-o",
+           str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stderr}")
@@ -55,6 +71,8 @@ def sources() -> list[Path]:
 
 def up_to_date() -> bool:
     if not LIB.exists():
+        return False
+    if (STAMP.read_text() if STAMP.exists() else "") != " ".join(extra_defines()):
         return False
     t = LIB.stat().st_mtime
     deps = list(CSRC.glob("*")) + [PKG.parent / "include" / "cusort_b200.h", Path(__file__)]
@@ -80,6 +98,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
     os.replace(tmp, LIB)
+    STAMP.write_text(" ".join(extra_defines()))
     if verbose:
         print("".join(logs))
     return LIB

@@ -35,6 +35,13 @@ namespace cusort_b200 {
 #ifndef CUSORT_OS_KPT_K4V4
 #define CUSORT_OS_KPT_K4V4 16
 #endif
+// The staged kernel (routed multi-GPU partition passes, segmented passes, and
+// keys-only sorts of 1-2 byte keys) keeps the sizes it was tuned at: 36 items
+// per thread keys-only (32 -> 36: u32 keys-only sort 1.045 -> 1.026 ms), 20
+// for 8-byte items (16 -> 20: int32+uint32 pass 0.369 -> 0.356 ms).
+#ifndef CUSORT_OS_KPT_KEYS_STAGED
+#define CUSORT_OS_KPT_KEYS_STAGED 36
+#endif
 #ifndef CUSORT_OS_KPT_LE8
 #define CUSORT_OS_KPT_LE8 20
 #endif
@@ -90,7 +97,7 @@ namespace cusort_b200 {
 #define CUSORT_OS_KPT_MID_TILE 16
 #endif
 
-template <int KB, int VB>
+template <int KB, int VB, bool STAGED = false>
 struct TileShape {
   static constexpr int THREADS = CUSORT_OS_THREADS;
   static constexpr int BYTES = KB + VB;
@@ -101,8 +108,9 @@ struct TileShape {
                              : SMALLV                       ? CUSORT_OS_KPT_SMALLV
                              : (KB == 8 && VB == 16)  ? CUSORT_OS_KPT_K8V16
                              : (KB == 8 && VB == 8) ? CUSORT_OS_KPT_K8V8
+                             : (VB == 0 && KB <= 4 && (STAGED || KB < 4)) ? CUSORT_OS_KPT_KEYS_STAGED
                              : (VB == 0 && KB <= 4) ? CUSORT_OS_KPT_KEYS4
-                             : (KB == 4 && VB == 4) ? CUSORT_OS_KPT_K4V4
+                             : (KB == 4 && VB == 4 && !STAGED) ? CUSORT_OS_KPT_K4V4
                              : (BYTES > 16)         ? CUSORT_OS_KPT_GT16
                              : (BYTES > 8)          ? CUSORT_OS_KPT_LE16
                                                     : CUSORT_OS_KPT_LE8;
@@ -114,7 +122,7 @@ constexpr int kHistUnroll = 4;
 
 template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG = false>
 inline void fill_onesweep(KernelInfo* os) {
-  using S = TileShape<KB, VB>;
+  using S = TileShape<KB, VB, ROUTED || SEG>;
   using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>;
   if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);
   else os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);

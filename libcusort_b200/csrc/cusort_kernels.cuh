@@ -520,44 +520,6 @@ struct WarpCounters<4> : WarpCounters<3> {
     uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
     atomicAdd(cnt + (d >> 1), 1u << ((d & 1u) << 4));
   }
-  // Hot-digit variants.  `hot` is one digit holding a large share of the
-  // pass (from the upfront histogram).  Its lanes would serialize on one
-  // shared word in both the count and the match table, so they find each
-  // other with one ballot instead: the lowest of them adds the group's size,
-  // and the ranking takes the ballot as their peer set and skips the table.
-  __device__ __forceinline__ static void count_key_hot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t hot,
-                                                       uint32_t lt) {
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
-    const bool h = d == hot;
-    const uint32_t hm = __ballot_sync(0xffffffffu, h);
-    const uint32_t add = (h ? (uint32_t)__popc(hm) : 1u) << ((d & 1u) << 4);
-    dev::atom_add_shared_if(!h || (hm & lt) == 0u, cnt + (d >> 1), add, 0u);
-  }
-  template <int S>
-  __device__ __forceinline__ static uint32_t rank_slot_hot(uint8_t* tab, uint32_t warp, uint32_t d, uint32_t lane,
-                                                           uint32_t lt, uint32_t& prev_word, uint32_t hot) {
-    uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
-    uint32_t* cnt = base;
-    uint32_t* msk = base + kRadix / 2;
-    const bool h = d == hot;
-    const uint32_t hm = __ballot_sync(0xffffffffu, h);
-    const uint32_t word = (uint32_t)(S % NT) * MASK_WORDS + (d >> 2);
-    if (!h) atomicOr(msk + word, 1u << lane);
-    const uint32_t pl = dev::match_digit_ballot<2>(d);
-    __syncwarp();
-    const uint32_t ph = h ? hm : msk[word];
-    // previous slot's table: read by all lanes before the barrier above (a
-    // hot lane clears the word it would have used: zero either way)
-    if (S > 0) msk[prev_word] = 0u;
-    prev_word = word;
-    const uint32_t peers = h ? hm : (pl & ph);
-    const uint32_t below = __popc(peers & lt);
-    const uint32_t leader = 31u - __clz(peers);
-    const uint32_t sh = (d & 1u) << 4;
-    uint32_t old = dev::atom_add_shared_if(lane == leader, cnt + (d >> 1), (below + 1u) << sh, 0u);
-    old = __shfl_sync(0xffffffffu, old, leader);
-    return ((old >> sh) & 0xffffu) + below;
-  }
 };
 
 // Mode 5: mode 4's counting pre-pass and position counters with the peer set
@@ -635,8 +597,77 @@ struct WarpCounters32 {
     reinterpret_cast<uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = v;
   }
 };
+// Mode 9: mode 6 ranking two slots at a time.  Each slot's chain (table
+// atomicOr, warp barrier, table read, the leader's counter atomic, shuffle)
+// waits on shared-memory round trips; two slots with their own tables share
+// one warp barrier and overlap their round trips.  The two leaders' counter
+// atomics are issued in slot order, and shared-memory atomics of one warp take
+// effect in program order, so the second slot's positions follow the first's.
+// Four tables rotate: a pair uses two while it clears the previous pair's.
+struct WarpCounters32Pair {
+  static constexpr int NT = 4;
+  static constexpr size_t MASK_WORDS = 64;
+  static constexpr size_t BYTES_PER_WARP = kRadix * 4 + NT * MASK_WORDS * 4;
+  static_assert(BYTES_PER_WARP % 16 == 0, "16-byte zeroing");
+  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
+    uint4* w = reinterpret_cast<uint4*>(tab + (size_t)warp * BYTES_PER_WARP);
+    constexpr int V = (int)(BYTES_PER_WARP / 16);
+#pragma unroll
+    for (int i = 0; i < (V + 31) / 32; ++i)
+      if (i * 32 + (int)lane < V) w[lane + 32 * i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  __device__ __forceinline__ static void count_key(uint8_t* tab, uint32_t warp, uint32_t d) {
+    atomicAdd(reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP) + d, 1u);
+  }
+  // Ranks slots S and S+1 (digits d0, d1); returns their tile positions.
+  // prev0/prev1: the previous pair's table words of this lane (cleared here).
+  template <int S>
+  __device__ __forceinline__ static void rank_pair(uint8_t* tab, uint32_t warp, uint32_t d0, uint32_t d1, uint32_t lane,
+                                                   uint32_t lt, uint32_t& prev0, uint32_t& prev1, uint32_t& pos0,
+                                                   uint32_t& pos1) {
+    uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
+    uint32_t* cnt = base;
+    uint32_t* msk = base + kRadix;
+    constexpr uint32_t T0 = (uint32_t)(S % NT) * MASK_WORDS, T1 = (uint32_t)((S + 1) % NT) * MASK_WORDS;
+    const uint32_t w0 = T0 + (d0 >> 2), w1 = T1 + (d1 >> 2);
+    atomicOr(msk + w0, 1u << lane);
+    atomicOr(msk + w1, 1u << lane);
+    const uint32_t pl0 = dev::match_digit_ballot<2>(d0);
+    const uint32_t pl1 = dev::match_digit_ballot<2>(d1);
+    __syncwarp();
+    const uint32_t ph0 = msk[w0];
+    const uint32_t ph1 = msk[w1];
+    if (S > 0) {  // the previous pair's tables: read by all lanes before the barrier above
+      msk[prev0] = 0u;
+      msk[prev1] = 0u;
+    }
+    prev0 = w0;
+    prev1 = w1;
+    const uint32_t peers0 = pl0 & ph0, peers1 = pl1 & ph1;
+    const uint32_t below0 = __popc(peers0 & lt), below1 = __popc(peers1 & lt);
+    const uint32_t lead0 = 31u - __clz(peers0), lead1 = 31u - __clz(peers1);
+    uint32_t old0 = dev::atom_add_shared_if(lane == lead0, cnt + d0, below0 + 1u, 0u);
+    uint32_t old1 = dev::atom_add_shared_if(lane == lead1, cnt + d1, below1 + 1u, 0u);
+    old0 = __shfl_sync(0xffffffffu, old0, lead0);
+    old1 = __shfl_sync(0xffffffffu, old1, lead1);
+    pos0 = old0 + below0;
+    pos1 = old1 + below1;
+  }
+  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
+    return reinterpret_cast<const uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
+  }
+  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
+    reinterpret_cast<uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = v;
+  }
+};
+
 template <>
 struct WarpCounters<6> : WarpCounters32<2> {};
+template <>
+struct WarpCounters<9> : WarpCounters32Pair {};
 template <>
 struct WarpCounters<7> : WarpCounters32<1> {};
 template <>
@@ -736,45 +767,6 @@ struct OnesweepCfg {
 #define CUSORT_VSMEM_MAXKB 4
 #endif
   static constexpr bool VSMEM = CUSORT_VSMEM && VB_ > 0 && VB_ <= 2 && KB_ <= CUSORT_VSMEM_MAXKB;
-  // Routed passes' tables (layout below).
-  static constexpr size_t ROUTE_LAYOUT_BYTES =
-      ROUTED ? (kRadix + 4 * 8 * kMaxRouteRanks + 8 * (kRadix + 8) + 2 * 4 * kMaxRouteRanks + 2 * 8 * kRadix) : 0;
-  // Everything but the per-warp tables (one staging buffer).
-  static constexpr size_t NON_WTAB_BYTES = BUF_BYTES + 16 + kRadix * 4 + 2 * kRadix * sizeof(Off) + 16 * 4 + 32 +
-                                           (VSMEM ? align_up((size_t)TILE * VB, 16) : 0) + ROUTE_LAYOUT_BYTES;
-  // Rank mode (WarpCounters): the preferred one for the key/value width --
-  // measured on B200 at 2^26 items, the 32-bit counters of mode 6 beat the
-  // packed 16-bit counters of mode 4 for every 4-byte-key shape (2-5 % on
-  // uniform keys, 18-26 % on skewed ones) -- unless its larger tables would
-  // push the CTA past its share of shared memory (MINB CTAs per SM), where
-  // mode 4 keeps the tile shape's occupancy.
-  static constexpr int PREF_RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
-  static constexpr int RANK_MODE =
-      (PREF_RANK_MODE >= 6 && NON_WTAB_BYTES + (size_t)WARPS * WarpCounters<(PREF_RANK_MODE >= 6 ? PREF_RANK_MODE : 6)>::BYTES_PER_WARP >
-                                  SMEM_PER_CTA)
-          ? 4
-          : PREF_RANK_MODE;
-  using WC = WarpCounters<RANK_MODE>;
-  static constexpr size_t REST_BYTES = align_up((size_t)WARPS * WC::BYTES_PER_WARP, 16) + kRadix * 4 +
-                                       2 * kRadix * sizeof(Off) + 16 * 4 + 32;
-  // Mode 4 needs a key's digit twice (count, rank); recomputing it from the
-  // key instead of keeping a digit array frees KPT registers, which buys
-  // larger tiles (2 = every width, 1 = keys-only, 0 = never).
-#ifndef CUSORT_RECOMPUTE_DIGIT
-#define CUSORT_RECOMPUTE_DIGIT 2
-#endif
-  static constexpr bool RECOMPUTE_DIGIT =
-      RANK_MODE >= 4 && (CUSORT_RECOMPUTE_DIGIT == 2 || (CUSORT_RECOMPUTE_DIGIT == 1 && VB_ == 0));
-  // Hot-digit ranking (WarpCounters<4>::count_key_hot / rank_slot_hot) when
-  // a digit holds more than 1/CUSORT_HOT_SHARE of the pass's items; plain
-  // passes only (the counts come from the upfront histogram).
-#ifndef CUSORT_HOT_DIGIT
-#define CUSORT_HOT_DIGIT 0
-#endif
-#ifndef CUSORT_HOT_SHARE
-#define CUSORT_HOT_SHARE 16
-#endif
-  static constexpr bool HOT = CUSORT_HOT_DIGIT && RANK_MODE == 4 && !ROUTED_ && !SEG_;
   // Pipelined register loads (onesweep_pipe_kernel): the next tile's keys and
   // values are loaded from global memory straight into registers while the
   // current tile is scattered out of shared memory; no staging copy.
@@ -795,19 +787,40 @@ struct OnesweepCfg {
 #ifndef CUSORT_PIPE_MAXVB
 #define CUSORT_PIPE_MAXVB 4
 #endif
-  // Integer keys of plain passes: the twiddle of the pass's digit is a
-  // constant xor, a bijection on digits.  The per-warp tables, the ranking and
-  // the digit offsets used by the scatter are then indexed by the raw digit
-  // (key >> shift) & mask, and the xor moves into the per-tile scan (digit t's
-  // entries sit at t ^ (twiddle constant's digit)): one instruction less per
-  // digit computation, three per key.
-#ifndef CUSORT_FOLD_TWIDDLE
-#define CUSORT_FOLD_TWIDDLE 0
+  static constexpr bool PIPE_OK = CUSORT_PIPE && !ROUTED_ && !SEG_ && !VSMEM && !(CUSORT_PREFETCH != 0) &&
+                                  KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB && VB_ <= CUSORT_PIPE_MAXVB;
+  // Routed passes' tables (layout below).
+  static constexpr size_t ROUTE_LAYOUT_BYTES =
+      ROUTED ? (kRadix + 4 * 8 * kMaxRouteRanks + 8 * (kRadix + 8) + 2 * 4 * kMaxRouteRanks + 2 * 8 * kRadix) : 0;
+  // Everything but the per-warp tables (one staging buffer).
+  static constexpr size_t NON_WTAB_BYTES = BUF_BYTES + 16 + kRadix * 4 + 2 * kRadix * sizeof(Off) + 16 * 4 + 32 +
+                                           (VSMEM ? align_up((size_t)TILE * VB, 16) : 0) + ROUTE_LAYOUT_BYTES;
+  // Rank mode (WarpCounters): the preferred one for the key/value width --
+  // measured on B200 at 2^26 items, the 32-bit counters of mode 6 beat the
+  // packed 16-bit counters of mode 4 for every 4-byte-key shape (2-5 % on
+  // uniform keys, 18-26 % on skewed ones) -- unless its larger tables would
+  // push the CTA past its share of shared memory (MINB CTAs per SM), where
+  // mode 4 keeps the tile shape's occupancy.
+  // (mode 9 ranks slot pairs and exists in the pipelined kernel only)
+  static constexpr int PREF_MODE_0 = CUSORT_RANK_MODE_OF(KB_, VB_);
+  static constexpr int PREF_RANK_MODE = (PREF_MODE_0 == 9 && !PIPE_OK) ? 6 : PREF_MODE_0;
+  static constexpr int RANK_MODE =
+      (PREF_RANK_MODE >= 6 && NON_WTAB_BYTES + (size_t)WARPS * WarpCounters<(PREF_RANK_MODE >= 6 ? PREF_RANK_MODE : 6)>::BYTES_PER_WARP >
+                                  SMEM_PER_CTA)
+          ? 4
+          : PREF_RANK_MODE;
+  using WC = WarpCounters<RANK_MODE>;
+  static constexpr size_t REST_BYTES = align_up((size_t)WARPS * WC::BYTES_PER_WARP, 16) + kRadix * 4 +
+                                       2 * kRadix * sizeof(Off) + 16 * 4 + 32;
+  // Mode 4 needs a key's digit twice (count, rank); recomputing it from the
+  // key instead of keeping a digit array frees KPT registers, which buys
+  // larger tiles (2 = every width, 1 = keys-only, 0 = never).
+#ifndef CUSORT_RECOMPUTE_DIGIT
+#define CUSORT_RECOMPUTE_DIGIT 2
 #endif
-  static constexpr bool FOLD = CUSORT_FOLD_TWIDDLE && !FLOAT_KEY_ && !ROUTED_ && !SEG_;
-  static constexpr bool PIPE = CUSORT_PIPE && !ROUTED_ && !SEG_ && !VSMEM && !PREFETCH && !HOT &&
-                               RANK_MODE >= 4 && KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB &&
-                               VB_ <= CUSORT_PIPE_MAXVB;
+  static constexpr bool RECOMPUTE_DIGIT =
+      RANK_MODE >= 4 && (CUSORT_RECOMPUTE_DIGIT == 2 || (CUSORT_RECOMPUTE_DIGIT == 1 && VB_ == 0));
+  static constexpr bool PIPE = PIPE_OK && RANK_MODE >= 4;
   static constexpr int NBUF = (PREFETCH && 2 * BUF_BYTES + REST_BYTES <= SMEM_PER_CTA) ? 2 : 1;
   static constexpr size_t OFF_WTAB = NBUF * BUF_BYTES;
   static constexpr size_t OFF_TSTART = align_up(OFF_WTAB + (size_t)WARPS * WC::BYTES_PER_WARP, 16);
@@ -982,13 +995,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
   uint32_t num_tiles = a.num_tiles;  // segmented: the planner's count, read after the PDL wait
   const bool tma_ok = a.tma_keys && (!HAS_V || a.tma_vals);
   const uint64_t pol = dev::l2_policy_evict_first();
-  // digit of a key as the tables index it (the raw digit when CFG::FOLD; cx
-  // maps a digit to its table index and back)
-  const uint32_t cx = CFG::FOLD ? (uint32_t)((unsigned long long)tc >> a.shift) & a.mask : 0u;
-  auto kdigit = [&](K k) -> uint32_t {
-    if constexpr (CFG::FOLD) return (uint32_t)(k >> a.shift) & a.mask;
-    else return dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
-  };
+  auto kdigit = [&](K k) -> uint32_t { return dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask); };
 
   // A tile is staged by TMA when it is full and both inputs are 16-byte aligned.
   auto tma_tile = [&](uint32_t t) {
@@ -1010,8 +1017,6 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     return true;
   };
 
-  // [12..13]: the pass's hot digit, (count << 8 | digit) as u64, 0 if none
-  unsigned long long* s_hot = reinterpret_cast<unsigned long long*>(s_misc + 12);
   constexpr bool TIMED = CUSORT_LOOKBACK_TIMER && !CFG::ROUTED && !CFG::SEG;
   LookbackTimer lbt;
   if (tid == 0) {
@@ -1020,7 +1025,6 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     dev::fence_mbar_init();
     s_misc[2] = 0;
     s_misc[3] = 0;
-    *s_hot = 0ull;
     s_misc[14] = 0;  // lookback timer: the tile's maxima
     s_misc[15] = 0;
   }
@@ -1068,9 +1072,6 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       Off pre = 0;
       for (uint32_t w = 0; w < warp; ++w) pre += s_goff[w];
       s_gbase[tid] = pre + incl - cv;
-      if constexpr (CFG::HOT) {
-        if ((uint64_t)cv * CUSORT_HOT_SHARE > a.n) atomicMax(s_hot, ((unsigned long long)cv << 8) | tid);
-      }
     }
   }
   uint32_t cur = s_misc[0];
@@ -1177,7 +1178,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     // digit of slot s (the top digit for slots past the end of the tile)
     auto digit_at = [&](int s) -> uint32_t {
       const uint32_t idx = wfirst_c + s * 32 + lane;
-      return (idx < valid) ? kdigit(key[s]) : (a.mask ^ cx);
+      return (idx < valid) ? kdigit(key[s]) : a.mask;
     };
     V val[VREG ? KPT : 1];
     const uint32_t wfirst = wfirst_c;
@@ -1215,16 +1216,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
     uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
     constexpr bool EARLY = CFG::RANK_MODE >= 4;
-    // the pass's hot digit (256: none); written before the first tile's barrier
-    const uint32_t hot = (CFG::HOT && *s_hot != 0ull) ? ((uint32_t)(*s_hot & 0xffu) ^ cx) : 256u;
     if constexpr (EARLY) {
-      if (__builtin_expect(!CFG::HOT || hot >= 256u, 1)) {
 #pragma unroll
-        for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
-      } else if constexpr (CFG::HOT) {
-#pragma unroll
-        for (int s = 0; s < KPT; ++s) WC::count_key_hot(s_wtab, warp, RECOMP ? digit_at(s) : dr[s], hot, lt);
-      }
+      for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
     } else {
       static_assert(!RECOMP, "digit recomputation needs the early-count rank modes");
       uint32_t prev = 0;
@@ -1237,8 +1231,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     if (tid < kRadix) {
 #pragma unroll 4
       for (int w = 0; w < WARPS; ++w) {
-        const uint32_t c = WC::count(s_wtab, w, tid ^ cx);
-        WC::put(s_wtab, w, tid ^ cx, cnt);
+        const uint32_t c = WC::count(s_wtab, w, tid);
+        WC::put(s_wtab, w, tid, cnt);
         cnt += c;
       }
       if (tid == a.mask) cnt -= (uint32_t)TILE - valid;
@@ -1258,7 +1252,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       const uint32_t ts = pre + incl - cnt;
       s_tstart[tid] = ts;
 #pragma unroll 4
-      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid ^ cx, WC::get(s_wtab, w, tid ^ cx) + ts);
+      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
     }
     __syncthreads();
 
@@ -1277,17 +1271,10 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
           }
         };
         uint32_t prev = 0;
-        if (__builtin_expect(!CFG::HOT || hot >= 256u, 1)) {
-          static_for<0, KPT>([&](auto sc) {
-            constexpr int S = decltype(sc)::value;
-            store(sc, WC::template rank_slot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev));
-          });
-        } else if constexpr (CFG::HOT) {
-          static_for<0, KPT>([&](auto sc) {
-            constexpr int S = decltype(sc)::value;
-            store(sc, WC::template rank_slot_hot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev, hot));
-          });
-        }
+        static_for<0, KPT>([&](auto sc) {
+          constexpr int S = decltype(sc)::value;
+          store(sc, WC::template rank_slot<S>(s_wtab, warp, RECOMP ? digit_at(S) : dr[S], lane, lt, prev));
+        });
       } else {
 #pragma unroll
         for (int s = 0; s < KPT; ++s) {
@@ -1325,7 +1312,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         s_pre[tid] = incl_x;
         if (lane == 31) s_pre[kRadix + warp] = incl_x;
       } else {
-        s_goff[tid ^ cx] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+        s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
     }
     reorder();
@@ -1437,12 +1424,6 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
 #ifndef CUSORT_PIPE_SCATTER_UNROLL
 #define CUSORT_PIPE_SCATTER_UNROLL 4
 #endif
-#ifndef CUSORT_LOOKBACK_LATE
-#define CUSORT_LOOKBACK_LATE 0
-#endif
-#ifndef CUSORT_LOOKBACK_LATE_WINDOW
-#define CUSORT_LOOKBACK_LATE_WINDOW 16
-#endif
 // Issues the global loads of tile t for one thread (slot s = item first + 32 s
 // of the tile) into registers; slots past the end get the sentinel key.
 template <class CFG, typename K, typename V, int NV>
@@ -1497,11 +1478,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
   // bit is set (the key's own sign bit is then clear), else ~(c ^ f)
   constexpr int NB = CFG::KB * 8;
   const K sentinel = ((tc >> (NB - 1)) & 1) ? (K)~tc : (K)~(tc ^ tf);
-  const uint32_t cx = CFG::FOLD ? (uint32_t)((unsigned long long)tc >> a.shift) & a.mask : 0u;
-  auto kdigit = [&](K k) -> uint32_t {
-    if constexpr (CFG::FOLD) return (uint32_t)(k >> a.shift) & a.mask;
-    else return dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
-  };
+  auto kdigit = [&](K k) -> uint32_t { return dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask); };
   const K* keys_in = static_cast<const K*>(a.keys_in);
   K* keys_out = static_cast<K*>(a.keys_out);
   const V* vals_in = static_cast<const V*>(a.vals_in);
@@ -1567,8 +1544,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     if (tid < kRadix) {
 #pragma unroll 4
       for (int w = 0; w < WARPS; ++w) {
-        const uint32_t c = WC::count(s_wtab, w, tid ^ cx);
-        WC::put(s_wtab, w, tid ^ cx, cnt);
+        const uint32_t c = WC::count(s_wtab, w, tid);
+        WC::put(s_wtab, w, tid, cnt);
         cnt += c;
       }
       if (tid == a.mask) cnt -= (uint32_t)TILE - valid;  // the sentinels
@@ -1588,18 +1565,15 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
       const uint32_t ts = pre + incl - cnt;
       s_tstart[tid] = ts;
 #pragma unroll 4
-      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid ^ cx, WC::get(s_wtab, w, tid ^ cx) + ts);
+      for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
     }
     __syncthreads();
 
-    // ---- decoupled lookback and rank + reorder.  CUSORT_LOOKBACK_LATE = 0:
-    // the digit-owning warps look back first (their L2 round trips overlap
-    // the other warps' reordering) with a window small enough to fit beside
-    // the tile's keys in registers; 1: after their own reordering, when the
-    // keys' registers are free, with a window of CUSORT_LOOKBACK_LATE_WINDOW
-    // predecessors, so that one round usually reaches an inclusive word.
-    auto lookback = [&](auto window_tag) {
-      constexpr int W = decltype(window_tag)::value;
+    // ---- decoupled lookback and rank + reorder: the digit-owning warps look
+    // back first, so their L2 round trips overlap the other warps' reordering
+    // (with a window small enough to fit beside the tile's keys in registers)
+    {
+      constexpr int W = lookback_window<Off>();
       if (tid < kRadix) {
         Off excl = 0;
         if (tile > 0) {
@@ -1611,26 +1585,37 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
           if (publish)
             dev::st_relaxed(desc + (size_t)tile * kRadix + tid, DB::make(a.pass, kDescInclusive, excl + (Off)cnt));
         }
-        s_goff[tid ^ cx] = s_gbase[tid] + excl - (Off)s_tstart[tid];
+        s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
-    };
-    if constexpr (!CUSORT_LOOKBACK_LATE) lookback(std::integral_constant<int, lookback_window<Off>()>{});
+    }
     {
-      uint32_t prev = 0;
-      static_for<0, KPT>([&](auto sc) {
+      auto store = [&](auto sc, uint32_t pos) {
         constexpr int S = decltype(sc)::value;
-        const uint32_t pos = WC::template rank_slot<S>(s_wtab, warp, digit(S), lane, lt, prev);
         if constexpr (CFG::PACKED_KV) {
           s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
         } else {
           s_keys[pos] = key[S];
           if constexpr (HAS_V) s_vals[pos] = val[S];
         }
-      });
+      };
+      if constexpr (CFG::RANK_MODE == 9) {
+        static_assert(KPT % 2 == 0, "pairwise ranking: an even number of slots");
+        uint32_t prev0 = 0, prev1 = 0;
+        static_for<0, KPT / 2>([&](auto pc) {
+          constexpr int S = 2 * decltype(pc)::value;
+          uint32_t p0, p1;
+          WC::template rank_pair<S>(s_wtab, warp, digit(S), digit(S + 1), lane, lt, prev0, prev1, p0, p1);
+          store(std::integral_constant<int, S>{}, p0);
+          store(std::integral_constant<int, S + 1>{}, p1);
+        });
+      } else {
+        uint32_t prev = 0;
+        static_for<0, KPT>([&](auto sc) {
+          constexpr int S = decltype(sc)::value;
+          store(sc, WC::template rank_slot<S>(s_wtab, warp, digit(S), lane, lt, prev));
+        });
+      }
     }
-    if constexpr (CUSORT_LOOKBACK_LATE)
-      lookback(std::integral_constant<int, sizeof(Off) == 8 ? CUSORT_LOOKBACK_LATE_WINDOW / 2
-                                                            : CUSORT_LOOKBACK_LATE_WINDOW>{});
     if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
     __syncthreads();
     if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
