@@ -597,77 +597,9 @@ struct WarpCounters32 {
     reinterpret_cast<uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = v;
   }
 };
-// Mode 9: mode 6 ranking two slots at a time.  Each slot's chain (table
-// atomicOr, warp barrier, table read, the leader's counter atomic, shuffle)
-// waits on shared-memory round trips; two slots with their own tables share
-// one warp barrier and overlap their round trips.  The two leaders' counter
-// atomics are issued in slot order, and shared-memory atomics of one warp take
-// effect in program order, so the second slot's positions follow the first's.
-// Four tables rotate: a pair uses two while it clears the previous pair's.
-struct WarpCounters32Pair {
-  static constexpr int NT = 4;
-  static constexpr size_t MASK_WORDS = 64;
-  static constexpr size_t BYTES_PER_WARP = kRadix * 4 + NT * MASK_WORDS * 4;
-  static_assert(BYTES_PER_WARP % 16 == 0, "16-byte zeroing");
-  __device__ __forceinline__ static void zero(uint8_t* tab, uint32_t warp, uint32_t lane) {
-    uint4* w = reinterpret_cast<uint4*>(tab + (size_t)warp * BYTES_PER_WARP);
-    constexpr int V = (int)(BYTES_PER_WARP / 16);
-#pragma unroll
-    for (int i = 0; i < (V + 31) / 32; ++i)
-      if (i * 32 + (int)lane < V) w[lane + 32 * i] = make_uint4(0u, 0u, 0u, 0u);
-  }
-  __device__ __forceinline__ static void count_key(uint8_t* tab, uint32_t warp, uint32_t d) {
-    atomicAdd(reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP) + d, 1u);
-  }
-  // Ranks slots S and S+1 (digits d0, d1); returns their tile positions.
-  // prev0/prev1: the previous pair's table words of this lane (cleared here).
-  template <int S>
-  __device__ __forceinline__ static void rank_pair(uint8_t* tab, uint32_t warp, uint32_t d0, uint32_t d1, uint32_t lane,
-                                                   uint32_t lt, uint32_t& prev0, uint32_t& prev1, uint32_t& pos0,
-                                                   uint32_t& pos1) {
-    uint32_t* base = reinterpret_cast<uint32_t*>(tab + (size_t)warp * BYTES_PER_WARP);
-    uint32_t* cnt = base;
-    uint32_t* msk = base + kRadix;
-    constexpr uint32_t T0 = (uint32_t)(S % NT) * MASK_WORDS, T1 = (uint32_t)((S + 1) % NT) * MASK_WORDS;
-    const uint32_t w0 = T0 + (d0 >> 2), w1 = T1 + (d1 >> 2);
-    atomicOr(msk + w0, 1u << lane);
-    atomicOr(msk + w1, 1u << lane);
-    const uint32_t pl0 = dev::match_digit_ballot<2>(d0);
-    const uint32_t pl1 = dev::match_digit_ballot<2>(d1);
-    __syncwarp();
-    const uint32_t ph0 = msk[w0];
-    const uint32_t ph1 = msk[w1];
-    if (S > 0) {  // the previous pair's tables: read by all lanes before the barrier above
-      msk[prev0] = 0u;
-      msk[prev1] = 0u;
-    }
-    prev0 = w0;
-    prev1 = w1;
-    const uint32_t peers0 = pl0 & ph0, peers1 = pl1 & ph1;
-    const uint32_t below0 = __popc(peers0 & lt), below1 = __popc(peers1 & lt);
-    const uint32_t lead0 = 31u - __clz(peers0), lead1 = 31u - __clz(peers1);
-    uint32_t old0 = dev::atom_add_shared_if(lane == lead0, cnt + d0, below0 + 1u, 0u);
-    uint32_t old1 = dev::atom_add_shared_if(lane == lead1, cnt + d1, below1 + 1u, 0u);
-    old0 = __shfl_sync(0xffffffffu, old0, lead0);
-    old1 = __shfl_sync(0xffffffffu, old1, lead1);
-    pos0 = old0 + below0;
-    pos1 = old1 + below1;
-  }
-  __device__ __forceinline__ static uint32_t count(const uint8_t* tab, uint32_t w, uint32_t t) {
-    return reinterpret_cast<const uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
-  }
-  __device__ __forceinline__ static uint32_t get(const uint8_t* tab, uint32_t w, uint32_t t) {
-    return reinterpret_cast<const uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t];
-  }
-  __device__ __forceinline__ static void put(uint8_t* tab, uint32_t w, uint32_t t, uint32_t v) {
-    reinterpret_cast<uint32_t*>(tab + (size_t)w * BYTES_PER_WARP)[t] = v;
-  }
-};
-
 template <>
 struct WarpCounters<6> : WarpCounters32<2> {};
-template <>
-struct WarpCounters<9> : WarpCounters32Pair {};
+
 template <>
 struct WarpCounters<7> : WarpCounters32<1> {};
 template <>
@@ -801,9 +733,7 @@ struct OnesweepCfg {
   // uniform keys, 18-26 % on skewed ones) -- unless its larger tables would
   // push the CTA past its share of shared memory (MINB CTAs per SM), where
   // mode 4 keeps the tile shape's occupancy.
-  // (mode 9 ranks slot pairs and exists in the pipelined kernel only)
-  static constexpr int PREF_MODE_0 = CUSORT_RANK_MODE_OF(KB_, VB_);
-  static constexpr int PREF_RANK_MODE = (PREF_MODE_0 == 9 && !PIPE_OK) ? 6 : PREF_MODE_0;
+  static constexpr int PREF_RANK_MODE = CUSORT_RANK_MODE_OF(KB_, VB_);
   static constexpr int RANK_MODE =
       (PREF_RANK_MODE >= 6 && NON_WTAB_BYTES + (size_t)WARPS * WarpCounters<(PREF_RANK_MODE >= 6 ? PREF_RANK_MODE : 6)>::BYTES_PER_WARP >
                                   SMEM_PER_CTA)
@@ -1598,23 +1528,11 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
           if constexpr (HAS_V) s_vals[pos] = val[S];
         }
       };
-      if constexpr (CFG::RANK_MODE == 9) {
-        static_assert(KPT % 2 == 0, "pairwise ranking: an even number of slots");
-        uint32_t prev0 = 0, prev1 = 0;
-        static_for<0, KPT / 2>([&](auto pc) {
-          constexpr int S = 2 * decltype(pc)::value;
-          uint32_t p0, p1;
-          WC::template rank_pair<S>(s_wtab, warp, digit(S), digit(S + 1), lane, lt, prev0, prev1, p0, p1);
-          store(std::integral_constant<int, S>{}, p0);
-          store(std::integral_constant<int, S + 1>{}, p1);
-        });
-      } else {
-        uint32_t prev = 0;
-        static_for<0, KPT>([&](auto sc) {
-          constexpr int S = decltype(sc)::value;
-          store(sc, WC::template rank_slot<S>(s_wtab, warp, digit(S), lane, lt, prev));
-        });
-      }
+      uint32_t prev = 0;
+      static_for<0, KPT>([&](auto sc) {
+        constexpr int S = decltype(sc)::value;
+        store(sc, WC::template rank_slot<S>(s_wtab, warp, digit(S), lane, lt, prev));
+      });
     }
     if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
     __syncthreads();
