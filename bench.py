@@ -577,12 +577,50 @@ def seg_call(torch, keys, vals, kout, vout, seglen, stream):
     return call
 
 
+def composite_baselines(torch, keys, vals, kout_seg, vout_seg, seglen, stream):
+    """ms per sort of the segmented problem as ONE stable sort of (segment << 32 | twiddled key):
+    torch.sort(stable=True), and this library's uint64 SortPairs over bits [0, 32 + segment
+    bits); both checked equal to the segmented sort's output (kout_seg / vout_seg)."""
+    n = keys.numel()
+    segbits = max(1, int((n - 1) // seglen).bit_length())
+    seg = torch.arange(n, dtype=torch.int64, device=keys.device) // seglen
+    out = {}
+
+    def composite():
+        return (seg << 32) | ((keys.to(torch.int64) + 2 ** 31) & 0xFFFFFFFF)
+
+    def torch_way():
+        c = composite()
+        r = torch.sort(c, stable=True)
+        return r.values, vals[r.indices]
+    ms = time_steps(torch, torch_way, 5, 2) / 5
+    _, tv = torch_way()
+    out["torch_sort_stable"] = {"ms": round(ms, 4), "same_values": bool(torch.equal(tv, vout_seg))}
+    ck = composite()
+    ck_out = torch.empty_like(ck)
+    vin, v_out = vals.clone(), torch.empty_like(vals)
+    s = Sorter("ours", torch, "u64", 6, 8, 4, n, ck, ck_out, vin, v_out, stream, begin_bit=0, end_bit=32 + segbits)
+
+    def ours_way():
+        ck.copy_(composite())
+        s()
+    ms = time_steps(torch, ours_way, 5, 2) / 5
+    out["cusort_u64_pairs"] = {"ms": round(ms, 4), "bits": 32 + segbits, "same_values": bool(torch.equal(v_out, vout_seg))}
+    del seg, ck, ck_out, vin, v_out, s
+    return out
+
+
 def segmented(args, torch, device):
     """Segmented sort (CUB DeviceSegmentedRadixSort semantics; the reference has none) of 2^26
     int32 keys + uint32 index values in equal-length segments, one entry per length class: the
     warp all-pairs class (16), the warp and CTA shared-memory classes (1000, 4000) and the
     segmented onesweep (2^20).  3 warm-up + 10 timed sorts each; inputs > L2.  The first and
-    last segment of each timed output are checked against torch's stable sort."""
+    last segment of each timed output are checked against torch's stable sort.
+
+    Beside each, the same result through one stable sort of a composite 64-bit key (segment
+    index in the bits above the 32 key bits; what a caller without a segmented sort would do),
+    timed including the kernel that builds the composite key: with torch.sort(stable=True)
+    (torch's own GPU sort) and with this library's 64-bit SortPairs over only the bits in use."""
     n = 1 << args.log2n
     res = {}
     try:
@@ -603,6 +641,8 @@ def segmented(args, torch, device):
                                                                                        vout[a0:a1]))
             res[f"seglen_{seglen}"] = {"segments": call.segments, "ms_per_step": round(ms, 4),
                                        "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2), "checked": ok}
+            res[f"seglen_{seglen}"]["composite_key_baselines_ms"] = composite_baselines(
+                torch, keys, vals, kout, vout, seglen, stream)
         return res
     except Exception as e:  # informational leg: keep the headline line
         res["error"] = f"{type(e).__name__}: {e}"

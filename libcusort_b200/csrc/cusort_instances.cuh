@@ -122,7 +122,7 @@ constexpr int kHistUnroll = 4;
 
 template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG = false>
 inline void fill_onesweep(KernelInfo* os) {
-  using S = TileShape<KB, VB, ROUTED || SEG>;
+  using S = TileShape<KB, VB, ROUTED || SEG || (sizeof(Off) == 8 && !CUSORT_PIPE_WIDE_OFFSETS)>;
   using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>;
   if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);
   else os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);

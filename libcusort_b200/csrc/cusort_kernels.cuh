@@ -719,8 +719,13 @@ struct OnesweepCfg {
 #ifndef CUSORT_PIPE_MAXVB
 #define CUSORT_PIPE_MAXVB 4
 #endif
+// 64-bit offsets (2^30 items and more) in the pipelined kernel as well
+#ifndef CUSORT_PIPE_WIDE_OFFSETS
+#define CUSORT_PIPE_WIDE_OFFSETS 1
+#endif
   static constexpr bool PIPE_OK = CUSORT_PIPE && !ROUTED_ && !SEG_ && !VSMEM && !(CUSORT_PREFETCH != 0) &&
-                                  KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB && VB_ <= CUSORT_PIPE_MAXVB;
+                                  KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB && VB_ <= CUSORT_PIPE_MAXVB &&
+                                  (sizeof(Off_) == 4 || CUSORT_PIPE_WIDE_OFFSETS);
   // Routed passes' tables (layout below).
   static constexpr size_t ROUTE_LAYOUT_BYTES =
       ROUTED ? (kRadix + 4 * 8 * kMaxRouteRanks + 8 * (kRadix + 8) + 2 * 4 * kMaxRouteRanks + 2 * 8 * kRadix) : 0;
@@ -784,6 +789,9 @@ struct OnesweepCfg {
 #ifndef CUSORT_LOOKBACK_WINDOW
 #define CUSORT_LOOKBACK_WINDOW 8
 #endif
+#ifndef CUSORT_LOOKBACK_BACKOFF_NS
+#define CUSORT_LOOKBACK_BACKOFF_NS 0
+#endif
 template <typename Off>
 constexpr int lookback_window() {
   return sizeof(Off) == 8 ? CUSORT_LOOKBACK_WINDOW / 2 : CUSORT_LOOKBACK_WINDOW;
@@ -838,6 +846,11 @@ __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, u
     if (done) break;
     j -= consumed;
     if (empties && consumed == 0) ++*empties;
+    if constexpr (CUSORT_LOOKBACK_BACKOFF_NS > 0) {
+      // the nearest predecessor has published nothing yet: step back from
+      // the descriptor lines that many CTAs poll
+      if (consumed == 0) __nanosleep(CUSORT_LOOKBACK_BACKOFF_NS);
+    }
     if (consumed == 0 && guard.expired(status, limit_ns)) {
       atomicOr(status, kStatusLookbackTimeout);
       break;
