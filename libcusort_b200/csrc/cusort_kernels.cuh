@@ -214,15 +214,26 @@ __global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
   const uint64_t nvec = (a.n - head) / 8;
   const uint4* vec = reinterpret_cast<const uint4*>(keys + head);
   const uint64_t stride = (uint64_t)parts * 1024;
-  for (uint64_t v = (uint64_t)part * 1024 + tid; v < nvec; v += stride) {
-    const uint4 x = dev::ld_stream_v4(vec + v);
+  auto count_vec = [&](const uint4& x) {
     const uint32_t w[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       count(w[e] & 0xffffu);
       count(w[e] >> 16);
     }
+  };
+  // four independent 16-byte loads in flight per thread (one CTA of 1024
+  // threads per SM: with one load each, DRAM latency capped the read rate)
+  constexpr int U = 4;
+  uint64_t v = (uint64_t)part * 1024 + tid;
+  for (; v + (U - 1) * stride < nvec; v += U * stride) {
+    uint4 x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) x[u] = dev::ld_stream_v4(vec + v + u * stride);
+#pragma unroll
+    for (int u = 0; u < U; ++u) count_vec(x[u]);
   }
+  for (; v < nvec; v += stride) count_vec(dev::ld_stream_v4(vec + v));
   if (part == 0) {
     for (uint64_t i = tid; i < head; i += 1024) count(keys[i]);
     for (uint64_t i = head + nvec * 8 + tid; i < a.n; i += 1024) count(keys[i]);
@@ -719,9 +730,13 @@ struct OnesweepCfg {
 #ifndef CUSORT_PIPE_MAXVB
 #define CUSORT_PIPE_MAXVB 4
 #endif
-// 64-bit offsets (2^30 items and more) in the pipelined kernel as well
+// 64-bit offsets (2^30 items and more) keep the staged kernel: with 64-bit
+// descriptor words the lookback window is half as wide, and the pipelined
+// kernel's smaller tiles mean more tiles to look back over.  Measured on B200
+// (ms per sort, pipelined -> staged): 2^30 int32+uint32 pairs 23.5 -> 21.7,
+// 2^30 int32 keys 15.5 -> 14.5, 2^31 pairs 46.9 -> 43.3.
 #ifndef CUSORT_PIPE_WIDE_OFFSETS
-#define CUSORT_PIPE_WIDE_OFFSETS 1
+#define CUSORT_PIPE_WIDE_OFFSETS 0
 #endif
   static constexpr bool PIPE_OK = CUSORT_PIPE && !ROUTED_ && !SEG_ && !VSMEM && !(CUSORT_PREFETCH != 0) &&
                                   KB_ <= CUSORT_PIPE_MAXKB && KB_ >= CUSORT_PIPE_MINKB && VB_ <= CUSORT_PIPE_MAXVB &&
@@ -789,9 +804,6 @@ struct OnesweepCfg {
 #ifndef CUSORT_LOOKBACK_WINDOW
 #define CUSORT_LOOKBACK_WINDOW 8
 #endif
-#ifndef CUSORT_LOOKBACK_BACKOFF_NS
-#define CUSORT_LOOKBACK_BACKOFF_NS 0
-#endif
 template <typename Off>
 constexpr int lookback_window() {
   return sizeof(Off) == 8 ? CUSORT_LOOKBACK_WINDOW / 2 : CUSORT_LOOKBACK_WINDOW;
@@ -846,11 +858,6 @@ __device__ __forceinline__ Off lookback_prefix(const Off* desc, uint32_t tile, u
     if (done) break;
     j -= consumed;
     if (empties && consumed == 0) ++*empties;
-    if constexpr (CUSORT_LOOKBACK_BACKOFF_NS > 0) {
-      // the nearest predecessor has published nothing yet: step back from
-      // the descriptor lines that many CTAs poll
-      if (consumed == 0) __nanosleep(CUSORT_LOOKBACK_BACKOFF_NS);
-    }
     if (consumed == 0 && guard.expired(status, limit_ns)) {
       atomicOr(status, kStatusLookbackTimeout);
       break;
