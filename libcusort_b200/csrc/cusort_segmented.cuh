@@ -19,6 +19,8 @@
 //     segment's first tile).
 #pragma once
 
+#include <type_traits>
+
 #include "cusort_device.cuh"
 #include "cusort_types.h"
 
@@ -48,7 +50,8 @@ struct SegSmallLayout {
   static constexpr size_t VALS = ((size_t)CAP * (VB ? VB : 1) + 15) / 16 * 16;
   static constexpr size_t CNT = (size_t)WPS * kRadix * 4;
   static constexpr size_t SCAN = 16 * 4;
-  static constexpr size_t GROUP = KEYS + VALS + CNT + SCAN;
+  static constexpr size_t QUAL = 8 * 4;  // the qualifying segments of a chunk, one mask per warp
+  static constexpr size_t GROUP = KEYS + VALS + CNT + SCAN + QUAL;
   static constexpr int GROUPS = 8 / WPS;
   static constexpr size_t SMEM = GROUP * GROUPS;
 };
@@ -69,6 +72,7 @@ __global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a)
   V* sv = reinterpret_cast<V*>(gb + L::KEYS);
   uint32_t* cnt = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS);  // [WPS][256]
   uint32_t* scan = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS + L::CNT);
+  uint32_t* qual = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS + L::CNT + L::SCAN);
   auto gsync = [&]() {
     if constexpr (WPS == 1) __syncwarp();
     else __syncthreads();
@@ -80,12 +84,13 @@ __global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a)
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
   const uint32_t lt = dev::lanemask_lt();
 
-  const uint64_t groups = (uint64_t)gridDim.x * L::GROUPS;
-  for (uint64_t s = (uint64_t)blockIdx.x * L::GROUPS + g; s < a.num_segments; s += groups) {
+  auto length_of = [&](uint64_t s) -> uint64_t {
     const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
-    const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
-    if (len < a.min_len || len > a.max_len || len == 0) continue;  // uniform within the group
-    const uint32_t n = (uint32_t)len;
+    return e > b ? (uint64_t)(e - b) : 0;
+  };
+  auto sort_segment = [&](uint64_t s) {
+    const int64_t b = a.begin_offsets[s];
+    const uint32_t n = (uint32_t)length_of(s);
     for (uint32_t i = gtid; i < n; i += GT) {
       sk[i] = keys_in[b + i];
       if constexpr (HAS_V) sv[i] = vals_in[b + i];
@@ -172,6 +177,31 @@ __global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a)
       if constexpr (HAS_V) vals_out[b + i] = sv[i];
     }
     gsync();  // the buffers are reused by the next segment
+  };
+
+  // Group G owns segments G, G + groups, G + 2 groups, ...  It examines GT of
+  // them at a time, one per thread, and then sorts the ones of its length
+  // class in order: finding them costs one round trip per GT segments, not
+  // one per segment (with millions of short segments, mostly of other
+  // classes, that round trip dominated), and the work stays spread over the
+  // groups as before.
+  const uint64_t groups = (uint64_t)gridDim.x * L::GROUPS;
+  const uint64_t G = (uint64_t)blockIdx.x * L::GROUPS + g;
+  auto seg_at = [&](uint64_t base, uint32_t t) { return base + (uint64_t)t * groups + G; };
+  for (uint64_t base = 0; base + G < a.num_segments; base += groups * GT) {
+    const uint64_t mine = seg_at(base, gtid);
+    uint64_t len = 0;
+    if (mine < a.num_segments) len = length_of(mine);
+    const uint32_t qm = __ballot_sync(0xffffffffu, len != 0 && len >= a.min_len && len <= a.max_len);
+    if constexpr (WPS == 1) {
+      for (uint32_t m = qm; m; m &= m - 1) sort_segment(seg_at(base, (uint32_t)(__ffs(m) - 1)));
+    } else {
+      if (lane == 0) qual[wg] = qm;
+      __syncthreads();
+      for (int w = 0; w < WPS; ++w)
+        for (uint32_t m = qual[w]; m; m &= m - 1) sort_segment(seg_at(base, (uint32_t)w * 32 + (uint32_t)(__ffs(m) - 1)));
+      __syncthreads();  // every thread has read qual[] before it is rewritten
+    }
   }
 }
 
@@ -313,8 +343,20 @@ __global__ void __launch_bounds__(256) seg_tiny_kernel(const SegSmallArgs a) {
   const uint32_t nbits = 8u * (a.passes - 1u) + (uint32_t)__popc(a.last_mask);
   const unsigned long long range = nbits >= 64 ? ~0ull : ((1ull << nbits) - 1ull);
   const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
-  for (uint64_t s = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < a.num_segments; s += warps) {
-    const int64_t b = a.begin_offsets[s], e = a.end_offsets[s];
+  // the next segment's offsets are loaded while this one is sorted (one
+  // dependent round trip per segment instead of two)
+  uint64_t s = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int64_t nb = 0, ne = 0;
+  if (s < a.num_segments) {
+    nb = a.begin_offsets[s];
+    ne = a.end_offsets[s];
+  }
+  for (; s < a.num_segments; s += warps) {
+    const int64_t b = nb, e = ne;
+    if (s + warps < a.num_segments) {
+      nb = a.begin_offsets[s + warps];
+      ne = a.end_offsets[s + warps];
+    }
     const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
     if (len < a.min_len || len > a.max_len || len == 0) continue;  // uniform within the warp
     const uint32_t n = (uint32_t)len;
@@ -325,11 +367,12 @@ __global__ void __launch_bounds__(256) seg_tiny_kernel(const SegSmallArgs a) {
       k = keys_in[b + lane];
       if constexpr (HAS_V) v = vals_in[b + lane];
     }
-    const unsigned long long mk =
-        ((unsigned long long)dev::twiddle_k<FK, K>(k, tc, tf) >> a.begin_bit) & range;
+    // the masked key, compared as 32 bits when the key fits (one shuffle)
+    using M = typename std::conditional<(KB <= 4), uint32_t, unsigned long long>::type;
+    const M mk = (M)(((unsigned long long)dev::twiddle_k<FK, K>(k, tc, tf) >> a.begin_bit) & range);
     uint32_t rank = 0;
     for (uint32_t j = 0; j < n; ++j) {
-      const unsigned long long o = __shfl_sync(0xffffffffu, mk, j);
+      const M o = __shfl_sync(0xffffffffu, mk, j);
       rank += (o < mk || (o == mk && j < lane)) ? 1u : 0u;
     }
     if (in) {
