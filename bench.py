@@ -794,6 +794,19 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1 or args.gpus > 1:
+        if args.impl == "reference":
+            # The reference has no multi-GPU mode: rank 0 runs its single-GPU bench, the others exit.
+            if rank != 0:
+                return
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+            from oracle import oracle as O
+            if not O.ref_available():
+                print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libcusort_ref.so was not built"}))
+                return
+            out = run_single(args, torch)
+            out["note"] = "reference is single-GPU only: rank 0 ran the N=1 workload, other ranks idle"
+            print(json.dumps(out))
+            return
         from libcusort_b200 import mgpu_bench
         out = mgpu_bench.run(args, torch)
         if out is not None and rank == 0:

@@ -240,19 +240,6 @@ def run(args, torch):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        # The reference has no multi-GPU mode: rank 0 runs its single-GPU bench, the others exit.
-        if rank != 0:
-            return None
-        import bench
-        torch.cuda.set_device(local)
-        from oracle import oracle as O
-        if not O.ref_available():
-            return {"impl": "reference", "unavailable": "oracle/_ref/libcusort_ref.so was not built"}
-        out = bench.run_single(args, torch)
-        out["note"] = "reference is single-GPU only: rank 0 ran the N=1 workload, other ranks idle"
-        return out
-
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
