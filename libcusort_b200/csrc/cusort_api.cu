@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -145,6 +146,14 @@ struct Plan {
 constexpr size_t kCtrlBytes = 256;
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// CUSORT_WIDE_OFFSETS=1: every sort uses the 64-bit offset kernels that
+// 2^30 items and more select -- a test hook that checks those kernels against
+// the oracle on inputs it can sort.
+bool force_wide_offsets() {
+  const char* v = std::getenv("CUSORT_WIDE_OFFSETS");
+  return v && v[0] == '1';
+}
+
 static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int end, bool raw, Plan* p) {
   p->kt = kt;
   p->kb = key_bytes_of(kt);
@@ -154,7 +163,7 @@ static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int e
   p->begin = begin;
   p->end = end;
   // 30 count bits per descriptor word with 32-bit offsets (2 state bits).
-  p->offb = (n < (1ull << 30)) ? 4 : 8;
+  p->offb = (n < (1ull << 30) && !force_wide_offsets()) ? 4 : 8;
   const uint32_t nbits = (uint32_t)(end - begin);
   p->passes = (nbits + kRadixBits - 1) / kRadixBits;
   p->last_mask = (1u << (nbits - (p->passes - 1) * kRadixBits)) - 1u;
@@ -183,7 +192,7 @@ static bool make_plan(int kt, size_t vb, bool desc, uint64_t n, int begin, int e
     }
   }
   // Fewer items: smaller tiles, so the persistent grid still covers the SMs.
-  if (n <= kMidTileMaxItems) {
+  if (n <= kMidTileMaxItems && p->offb == 4) {
     KernelInfo small;
     if (get_small_onesweep(p->kb, p->vb, fk, n <= kSmallTileMaxItems ? 0 : 1, &small)) p->os = small;
   }

@@ -63,6 +63,10 @@ cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type
                                struct cusort_double_buffer* keys, struct cusort_double_buffer* values,
                                int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
 
+// CUSORT_WIDE_OFFSETS=1 in the environment: sorts of any size use the 64-bit
+// offset kernels (cusort_api.cu; a test hook).
+bool force_wide_offsets();
+
 // Single-digit counts (u64[256]) of the twiddled keys (cusort_api.cu).
 cudaError_t digit_counts_u64(int key_type, bool descending, const void* keys, int64_t num_items, int begin_bit,
                              int end_bit, unsigned long long* d_counts, cudaStream_t stream);

@@ -120,10 +120,29 @@ struct TileShape {
 constexpr int kHistThreads = 1024;
 constexpr int kHistUnroll = 4;
 
+// Largest items-per-thread count <= KPT at which the preferred rank mode's
+// per-warp tables still fit the CTA's share of shared memory.  Without it a
+// shape whose tables overflow keeps its tile and falls back to the packed
+// 16-bit counters of mode 4 -- and routed shapes overflowed the share even
+// then (one CTA per SM).  Measured on B200 (ms per sort, 64-bit offsets,
+// uint32 + uint32 pairs, 20 items per thread in mode 4 -> 19 in mode 6):
+// 2^31 uniform 43.3 -> 43.3, 2^31 Zipf(1.1) over 2^24 values 67.0 -> 50.5;
+// 2^30 uniform 21.7 -> 21.4, Zipf 33.5 -> 25.2.
+#ifndef CUSORT_FIT_RANK_MODE
+#define CUSORT_FIT_RANK_MODE 1
+#endif
+template <int KB, int VB, typename Off, int THREADS, int KPT, int MINB, bool FK, bool ROUTED, bool SEG>
+constexpr int fit_kpt() {
+  using CFG = OnesweepCfg<KB, VB, Off, THREADS, KPT, MINB, FK, ROUTED, SEG>;
+  if constexpr (!CUSORT_FIT_RANK_MODE || KPT <= 4 || CFG::RANK_MODE == CFG::PREF_RANK_MODE) return KPT;
+  else return fit_kpt<KB, VB, Off, THREADS, KPT - 1, MINB, FK, ROUTED, SEG>();
+}
+
 template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG = false>
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB, ROUTED || SEG || (sizeof(Off) == 8 && !CUSORT_PIPE_WIDE_OFFSETS)>;
-  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>;
+  constexpr int KPT = fit_kpt<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>();
+  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, KPT, S::MINB, FK, ROUTED, SEG>;
   if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);
   else os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;

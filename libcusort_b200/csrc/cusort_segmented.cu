@@ -133,7 +133,7 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
   const uint32_t nbits = (uint32_t)(end_bit - begin_bit);
   const uint32_t P = (nbits + 7) / 8;
   const uint32_t last_mask = P ? (1u << (nbits - (P - 1) * 8)) - 1u : 0u;
-  const int offb = ((uint64_t)n < (1ull << 30)) ? 4 : 8;
+  const int offb = ((uint64_t)n < (1ull << 30) && !force_wide_offsets()) ? 4 : 8;
   const bool fk = (kt == CUSORT_KEY_F32 || kt == CUSORT_KEY_F64);
   SegKernels k;
   bool ok = false;

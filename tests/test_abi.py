@@ -121,6 +121,23 @@ def test_offset_width_switch():
     assert p.value == 4
 
 
+def test_wide_offsets_hook(monkeypatch):
+    # CUSORT_WIDE_OFFSETS=1 (a test hook) selects the 64-bit offset kernels of 2^30+ items at any
+    # size, without the small-sort tile tiers (those kernels exist with 32-bit offsets only)
+    lib = _capi.load()
+    off, tile = C.c_int(0), C.c_int(0)
+    monkeypatch.setenv("CUSORT_WIDE_OFFSETS", "1")
+    assert lib.cusort_query_plan(4, 4, 1000, 0, 32, None, C.byref(tile), None, None, C.byref(off)) == 0
+    assert off.value == 8
+    # uint32 + uint32 with 64-bit offsets: 19 items per thread, the largest tile at which the 32-bit
+    # warp counters still fit two CTAs' share of shared memory
+    assert tile.value == 512 * 19
+    assert _tile_items(4, 0, 1000) == 512 * 36
+    monkeypatch.delenv("CUSORT_WIDE_OFFSETS")
+    assert lib.cusort_query_plan(4, 4, 1000, 0, 32, None, C.byref(tile), None, None, C.byref(off)) == 0
+    assert off.value == 4 and tile.value == 512 * 8
+
+
 def _tile_items(kt, vb, n):
     lib = _capi.load()
     t = C.c_int(0)
