@@ -311,7 +311,7 @@ static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers
     out->push_back(l);
   }
   if (p.fill16) {
-    // one 16-bit digit: count (CTA pairs split the bins), then fill the
+    // one 16-bit digit: count, then fill the
     // final destination (the last pass's output of the 8-bit schedule)
     Fill16Args f;
     f.keys = b.k_src[0];
@@ -325,7 +325,9 @@ static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers
     CUSORT_TRY(get_occupancy(dev, p.h16, &occ16));
     Launch l{};
     l.func = p.h16.func;
-    l.grid = 2 * (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ16 / 2, p.n / 16384 + 1));
+    const int readers = std::max(1, p.h16.tile);  // CTAs that read each key (a pair splits the bins)
+    l.grid = readers * (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * occ16 / readers,
+                                                                      p.n / (8192 * (uint64_t)readers) + 1));
     l.threads = p.h16.threads;
     l.smem = p.h16.smem;
     l.pdl = true;
@@ -334,7 +336,8 @@ static cudaError_t build_launches(const Plan& p, void* d_temp, const PassBuffers
     out->push_back(l);
     Launch l3{};
     l3.func = p.f16.func;
-    l3.grid = 256 * 4;
+    // the output split evenly: at least 32768 keys per CTA, at most 8 CTAs per SM
+    l3.grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * 8, (p.n + 32767) / 32768));
     l3.threads = p.f16.threads;
     l3.pdl = true;
     l3.kind = 2;

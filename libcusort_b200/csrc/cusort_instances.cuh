@@ -138,11 +138,26 @@ constexpr int fit_kpt() {
   else return fit_kpt<KB, VB, Off, THREADS, KPT - 1, MINB, FK, ROUTED, SEG>();
 }
 
+// Routed partition pass (multi-GPU): CTAs per SM, tile size in percent of
+// the plain staged shape's, and whether the tile is fitted to the 32-bit
+// warp counters (tuning knobs).
+#ifndef CUSORT_ROUTED_MINB
+#define CUSORT_ROUTED_MINB 2
+#endif
+#ifndef CUSORT_ROUTED_KPT_PCT
+#define CUSORT_ROUTED_KPT_PCT 100
+#endif
+#ifndef CUSORT_FIT_ROUTED
+#define CUSORT_FIT_ROUTED 1
+#endif
+
 template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG = false>
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB, ROUTED || SEG || (sizeof(Off) == 8 && !CUSORT_PIPE_WIDE_OFFSETS)>;
-  constexpr int KPT = fit_kpt<KB, VB, Off, S::THREADS, S::KPT, S::MINB, FK, ROUTED, SEG>();
-  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, KPT, S::MINB, FK, ROUTED, SEG>;
+  constexpr int MINB = ROUTED ? CUSORT_ROUTED_MINB : S::MINB;
+  constexpr int KPT0 = ROUTED ? S::KPT * CUSORT_ROUTED_KPT_PCT / 100 : S::KPT;
+  constexpr int KPT = (ROUTED && !CUSORT_FIT_ROUTED) ? KPT0 : fit_kpt<KB, VB, Off, S::THREADS, KPT0, MINB, FK, ROUTED, SEG>();
+  using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, KPT, MINB, FK, ROUTED, SEG>;
   if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);
   else os->func = reinterpret_cast<const void*>(&onesweep_kernel<CFG>);
   os->threads = CFG::THREADS;

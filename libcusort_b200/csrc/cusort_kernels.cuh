@@ -181,10 +181,16 @@ __global__ void __launch_bounds__(256) fill_bytes_kernel(const FillArgs a) {
 // ---------------------------------------------------------------------------
 // 16-bit digits for 16-bit keys-only sorts over all 16 bits (a one-pass
 // schedule: equal digits are equal keys, so counting is sorting).
-//   hist16_kernel: 1024-thread CTAs with 32768 shared u32 counters each; CTA
-//     pairs split the bins (blockIdx.x & 1 = top bit of the twiddled key) and
-//     the pairs split the keys (16-byte loads); at the end one global atomic
-//     per nonzero bin and one per group of 256 bins;
+//   hist16_kernel: one 1024-thread CTA per SM counts its share of the keys
+//     (16-byte loads, four in flight per thread) into all 65536 bins held as
+//     packed 16-bit counters (two bins per shared word, 128 KB).  The add
+//     that takes a half from 0x7fff to 0x8000 -- the only add that flips
+//     that half's top bit, since the half is brought back below 0x8000 right
+//     after -- moves 0x8000 of it to the global count, so a counter never
+//     carries into its neighbour.  At the end one global atomic per nonzero
+//     bin and one per nonzero group of 256 bins.  (CUSORT_HIST16_PACKED=0:
+//     32-bit counters, CTA pairs splitting the bins, every key read by both
+//     CTAs of a pair.)
 //   fill16_kernel: each CTA owns one group of 256 consecutive bins (a
 //     contiguous output range, a quarter of it per CTA): its start is the sum
 //     of the lower groups' totals, the bins' starts a 256-wide scan; it writes
@@ -192,22 +198,48 @@ __global__ void __launch_bounds__(256) fill_bytes_kernel(const FillArgs a) {
 //     contiguous shares.
 // ---------------------------------------------------------------------------
 constexpr int kBins16 = 65536;
+#ifndef CUSORT_HIST16_PACKED
+#define CUSORT_HIST16_PACKED 1
+#endif
+// CTAs that read each key: 1 with packed counters, 2 (a pair) with 32-bit ones
+constexpr int kHist16Readers = CUSORT_HIST16_PACKED ? 1 : 2;
 
 template <typename Off>
 __global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
   extern __shared__ __align__(16) uint32_t s_cnt16[];  // [32768]
+  __shared__ uint32_t s_grp[256];
+  constexpr bool PACKED = CUSORT_HIST16_PACKED != 0;
   dev::pdl_launch_dependents();
-  const uint32_t tid = threadIdx.x;
-  const uint32_t half = blockIdx.x & 1u;
-  const uint32_t part = blockIdx.x >> 1, parts = gridDim.x >> 1;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u;
+  const uint32_t half = PACKED ? 0u : (blockIdx.x & 1u);
+  const uint32_t part = PACKED ? blockIdx.x : (blockIdx.x >> 1);
+  const uint32_t parts = PACKED ? gridDim.x : (gridDim.x >> 1);
   for (uint32_t i = tid; i < kBins16 / 2; i += 1024) s_cnt16[i] = 0;
+  if (tid < 256) s_grp[tid] = 0;
+  Off* g = static_cast<Off*>(a.counts);
+  Off* gg = static_cast<Off*>(a.groups);
+  // packed counters move overflow chunks to the global counts while counting,
+  // so those must be zeroed (init kernel) first
+  if constexpr (PACKED) dev::pdl_wait();
   __syncthreads();
   const uint16_t* keys = static_cast<const uint16_t*>(a.keys);
   const uint32_t xc = a.xor_c & 0xffffu;
-  auto count = [&](uint32_t k) {
+  // m (< 0x8000) more copies of key k
+  auto count_m = [&](uint32_t k, uint32_t m) {
     const uint32_t t = (k ^ xc) & 0xffffu;
-    if ((t >> 15) == half) atomicAdd(s_cnt16 + (t & 0x7fffu), 1u);
+    if constexpr (PACKED) {
+      const uint32_t sh = (t & 1u) << 4, inc = m << sh;
+      const uint32_t old = atomicAdd(s_cnt16 + (t >> 1), inc);
+      if ((old ^ (old + inc)) & 0x80008000u) {
+        atomicSub(s_cnt16 + (t >> 1), 0x8000u << sh);
+        atomicAdd(g + t, (Off)0x8000u);
+        atomicAdd(gg + (t >> 8), (Off)0x8000u);
+      }
+    } else {
+      if ((t >> 15) == half) atomicAdd(s_cnt16 + (t & 0x7fffu), m);
+    }
   };
+  auto count = [&](uint32_t k) { count_m(k, 1u); };
   const uintptr_t addr = reinterpret_cast<uintptr_t>(keys);
   uint64_t head = ((16 - (addr & 15)) & 15) / 2;
   if (head > a.n) head = a.n;
@@ -226,10 +258,24 @@ __global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
   // threads per SM: with one load each, DRAM latency capped the read rate)
   constexpr int U = 4;
   uint64_t v = (uint64_t)part * 1024 + tid;
-  for (; v + (U - 1) * stride < nvec; v += U * stride) {
+  // while every lane of the warp has U vectors left (a warp-uniform test: the
+  // loop body uses warp collectives); the rest vector by vector
+  for (; (v - lane) + 31 + (U - 1) * stride < nvec; v += U * stride) {
     uint4 x[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) x[u] = dev::ld_stream_v4(vec + v + u * stride);
+    if constexpr (PACKED) {
+      // the warp's 32 x 8U keys all equal (one heavy value): one add for all,
+      // instead of 32-way same-address atomics
+      const uint32_t ref = __shfl_sync(0xffffffffu, x[0].x & 0xffffu, 0) * 0x10001u;
+      uint32_t d = 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u) d |= (x[u].x ^ ref) | (x[u].y ^ ref) | (x[u].z ^ ref) | (x[u].w ^ ref);
+      if (__all_sync(0xffffffffu, d == 0u)) {
+        if (lane == 0) count_m(ref & 0xffffu, 32u * 8u * U);
+        continue;
+      }
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) count_vec(x[u]);
   }
@@ -239,100 +285,202 @@ __global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
     for (uint64_t i = head + nvec * 8 + tid; i < a.n; i += 1024) count(keys[i]);
   }
   __syncthreads();
-  dev::pdl_wait();  // counts zeroed by the init kernel
-  // coalesced flush (a warp's 32 bins share one line); each warp's 32 bins lie
-  // in one group of 256, whose total is gathered in shared memory first
-  __shared__ uint32_t s_grp[128];
-  if (tid < 128) s_grp[tid] = 0;
-  __syncthreads();
-  Off* g = static_cast<Off*>(a.counts) + (size_t)half * (kBins16 / 2);
-  const uint32_t lane = tid & 31u;
+  if constexpr (!PACKED) dev::pdl_wait();  // counts zeroed by the init kernel
+  // coalesced flush (a warp's bins share one line); each warp's bins lie in
+  // one group of 256, whose total is gathered in shared memory first
   for (uint32_t i = tid; i < kBins16 / 2; i += 1024) {
     const uint32_t c = s_cnt16[i];
-    if (c) atomicAdd(g + i, (Off)c);
-    uint32_t w = c;
+    uint32_t w;
+    if constexpr (PACKED) {
+      const uint32_t lo = c & 0xffffu, hi = c >> 16;
+      if (lo) atomicAdd(g + 2 * i, (Off)lo);
+      if (hi) atomicAdd(g + 2 * i + 1, (Off)hi);
+      w = lo + hi;
+    } else {
+      if (c) atomicAdd(g + (size_t)half * (kBins16 / 2) + i, (Off)c);
+      w = c;
+    }
 #pragma unroll
     for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
-    if (lane == 0 && w) atomicAdd(s_grp + (i >> 8), w);
+    if (lane == 0 && w) atomicAdd(s_grp + (PACKED ? (i >> 7) : (half * 128 + (i >> 8))), w);
   }
   __syncthreads();
-  if (tid < 128 && s_grp[tid]) atomicAdd(static_cast<Off*>(a.groups) + half * 128 + tid, (Off)s_grp[tid]);
+  if (tid < 256 && s_grp[tid]) atomicAdd(gg + tid, (Off)s_grp[tid]);
 }
+
+// fill16_kernel: the output is split evenly over the CTAs whatever the key
+// distribution (a heavy value is written by every CTA its positions reach,
+// not by the one CTA that owns its bin).  A CTA walks its positions in
+// windows: a window's bin starts -- 2048 bins from a group boundary -- come
+// from a block-wide scan of their counts on top of the group starts (the
+// exclusive scan of the 256 group totals); the warps split the window's
+// 8-key vectors, lanes on consecutive vectors.
+constexpr int kFill16Chunk = 2048;
 
 template <typename Off>
 __global__ void __launch_bounds__(256) fill16_kernel(const Fill16Args a) {
-  __shared__ Off s_start[kRadix + 1];
-  __shared__ Off s_part[8];
+  __shared__ Off s_gstart[kRadix + 1];
+  __shared__ Off s_bs[kFill16Chunk + 1];
+  __shared__ Off s_wsum[8];
+  __shared__ unsigned long long s_w[2];
   dev::pdl_wait();  // counts from hist16_kernel
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  const uint32_t group = blockIdx.x >> 2, quarter = blockIdx.x & 3u;  // 256 groups of 256 bins
-  {
-    // group start = lower groups' totals; bin starts = exclusive scan of the counts
-    const Off gt = tid < group ? static_cast<const Off*>(a.groups)[tid] : Off(0);
-    const Off c = static_cast<const Off*>(a.counts)[(size_t)group * kRadix + tid];
-    Off gsum = gt;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) gsum += __shfl_xor_sync(0xffffffffu, gsum, o);
-    Off incl = c;
+  const Off* counts = static_cast<const Off*>(a.counts);
+  auto block_excl_scan = [&](Off v, Off* total) {  // all 256 threads
+    Off incl = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const Off t = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= (uint32_t)o) incl += t;
     }
-    if (lane == 0) s_start[warp] = gsum;  // temporary: warp sums of the group totals
-    if (lane == 31) s_part[warp] = incl;
+    if (lane == 31) s_wsum[warp] = incl;
     __syncthreads();
-    Off base = 0, pre = 0;
-    for (uint32_t w = 0; w < 8; ++w) base += s_start[w];
-    for (uint32_t w = 0; w < warp; ++w) pre += s_part[w];
-    __syncthreads();
-    s_start[tid] = base + pre + incl - c;
-    if (tid == kRadix - 1) s_start[kRadix] = base + pre + incl;
+    Off pre = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      pre += (w < (int)warp) ? s_wsum[w] : Off(0);
+      all += s_wsum[w];
+    }
+    __syncthreads();  // s_wsum is reused by the next scan
+    *total = all;
+    return pre + incl - v;
+  };
+  {
+    Off total;
+    const Off g = static_cast<const Off*>(a.groups)[tid];
+    s_gstart[tid] = block_excl_scan(g, &total);
+    if (tid == 0) s_gstart[kRadix] = total;
     __syncthreads();
   }
-  const uint64_t lo = s_start[0], hi = s_start[kRadix];
-  const uint64_t span = hi - lo, q0 = lo + span * quarter / 4, q1 = lo + span * (quarter + 1) / 4;
   uint16_t* out = static_cast<uint16_t*>(a.out);
   const uint32_t xc = a.xor_c & 0xffffu;
-  auto digit_at = [&](uint64_t i) {  // largest local bin b with start[b] <= i
-    uint32_t b = 0;
+  auto key_of = [&](uint32_t bin) { return (uint16_t)(bin ^ xc); };
+  auto group_of = [&](uint64_t p) {  // largest g with s_gstart[g] <= p (p < n)
+    uint32_t g = 0;
 #pragma unroll
     for (uint32_t step = 128; step; step >>= 1)
-      if ((uint64_t)s_start[b + step] <= i) b += step;
-    return b;
+      if ((uint64_t)s_gstart[g + step] <= p) g += step;
+    return g;
   };
-  auto key_of = [&](uint32_t b) { return (uint16_t)(((group << 8) | b) ^ xc); };
-  // unaligned head and ragged tail element by element
-  const uint64_t mis = (reinterpret_cast<uintptr_t>(out + q0) & 15) / 2;
-  uint64_t h = mis ? 8 - mis : 0;
-  if (h > q1 - q0) h = q1 - q0;
-  const uint64_t nvec = (q1 - q0 - h) / 8;
-  for (uint64_t i = q0 + tid; i < q0 + h; i += 256) out[i] = key_of(digit_at(i));
-  for (uint64_t i = q0 + h + nvec * 8 + tid; i < q1; i += 256) out[i] = key_of(digit_at(i));
-  // 8-key (16-byte) stores: each warp a contiguous share of the vectors, the
-  // lanes on consecutive vectors; a lane's bin only moves forward, so it is
-  // found once by binary search and then advanced
-  const uint64_t per = (nvec + 7) / 8, v0 = per * warp, v1 = v0 + per < nvec ? v0 + per : nvec;
-  const uint64_t p0 = q0 + h;
-  uint32_t b = 0;
-  bool found = false;
-  for (uint64_t v = v0 + lane; v < v1; v += 32) {
-    const uint64_t p = p0 + v * 8;
-    if (!found) {
-      b = digit_at(p);
-      found = true;
+  // bin of position p, the whole warp with the same p: the group's 256
+  // counts, 8 per lane, scanned across the lanes
+  auto bin_of = [&](uint64_t p) -> uint32_t {
+    const uint32_t g = group_of(p);
+    Off c[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      c[i] = counts[(size_t)g * kRadix + lane * 8 + i];
+      sum += c[i];
     }
-    while ((uint64_t)s_start[b + 1] <= p) ++b;
-    if ((uint64_t)s_start[b + 1] >= p + 8) {
-      const uint32_t k2 = (uint32_t)key_of(b) * 0x10001u;
-      *reinterpret_cast<uint4*>(out + p) = make_uint4(k2, k2, k2, k2);
-    } else {
-      uint32_t bb = b;
-      for (int e = 0; e < 8; ++e) {
-        while ((uint64_t)s_start[bb + 1] <= p + e) ++bb;
-        out[p + e] = key_of(bb);
+    Off incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const Off t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= (uint32_t)o) incl += t;
+    }
+    const uint64_t lo = (uint64_t)s_gstart[g] + (uint64_t)(incl - sum);
+    const bool mine = lo <= p && p < lo + (uint64_t)sum;
+    uint32_t e = 0;
+    if (mine) {
+      uint64_t at = lo;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (at <= p && p < at + (uint64_t)c[i]) e = (uint32_t)i;
+        at += (uint64_t)c[i];
       }
     }
+    const uint32_t who = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+    return g * kRadix + who * 8 + __shfl_sync(0xffffffffu, e, who);
+  };
+  const uint64_t n = a.n;
+  const uint64_t mis = (reinterpret_cast<uintptr_t>(out) & 15) / 2;
+  const uint64_t h = min(n, mis ? 8 - mis : (uint64_t)0);
+  const uint64_t nvec = (n - h) / 8, tail0 = h + nvec * 8;
+  // unaligned head (first CTA) and ragged tail (last CTA), element by element
+  if (warp == 0 && blockIdx.x == 0)
+    for (uint64_t i = 0; i < h; ++i) {
+      const uint32_t b = bin_of(i);
+      if (lane == 0) out[i] = key_of(b);
+    }
+  if (warp == 0 && blockIdx.x == gridDim.x - 1)
+    for (uint64_t i = tail0; i < n; ++i) {
+      const uint32_t b = bin_of(i);
+      if (lane == 0) out[i] = key_of(b);
+    }
+  const uint64_t p0 = h + 8 * (nvec * blockIdx.x / gridDim.x);
+  const uint64_t p1 = h + 8 * (nvec * (blockIdx.x + 1) / gridDim.x);
+  uint64_t w0 = p0;
+  while (w0 < p1) {
+    // window: the chunk of bins from the group of w0's bin
+    if (warp == 0) {
+      const uint32_t b = bin_of(w0);
+      if (lane == 0) s_w[0] = b & ~(uint32_t)(kRadix - 1);
+    }
+    __syncthreads();
+    const uint32_t cb = (uint32_t)s_w[0];
+    Off c[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t bin = cb + tid * 8 + i;
+      c[i] = bin < (uint32_t)kBins16 ? counts[bin] : Off(0);
+      sum += c[i];
+    }
+    Off total;
+    Off at = s_gstart[cb / kRadix] + block_excl_scan(sum, &total);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s_bs[tid * 8 + i] = at;
+      at += c[i];
+    }
+    if (tid == 0) s_bs[kFill16Chunk] = s_gstart[cb / kRadix] + total;
+    __syncthreads();
+    // vectors wholly inside the chunk's positions
+    uint64_t w1 = min(p1, (uint64_t)s_bs[kFill16Chunk]);
+    w1 = w1 > h ? h + (w1 - h) / 8 * 8 : h;
+    if (w1 <= w0) {
+      // one vector reaches past the chunk (empty bins between its keys): by element
+      if (warp == 0)
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t b = bin_of(w0 + e);
+          if (lane == 0) out[w0 + e] = key_of(b);
+        }
+      w0 += 8;
+      __syncthreads();  // s_w, s_bs reused
+      continue;
+    }
+    const uint64_t nv = (w1 - w0) / 8;
+    const uint64_t per = (nv + 7) / 8, u0 = min(nv, per * warp), u1 = min(nv, u0 + per);
+    uint32_t b = 0;
+    bool found = false;
+    for (uint64_t v = u0 + lane; v < u1; v += 32) {
+      const uint64_t p = w0 + v * 8;
+      if (!found) {  // largest local bin with start <= p
+        uint32_t lo = 0;
+#pragma unroll
+        for (uint32_t step = kFill16Chunk / 2; step; step >>= 1)
+          if ((uint64_t)s_bs[lo + step] <= p) lo += step;
+        b = lo;
+        found = true;
+      }
+      while ((uint64_t)s_bs[b + 1] <= p) ++b;
+      if ((uint64_t)s_bs[b + 1] >= p + 8) {
+        const uint32_t k2 = (uint32_t)key_of(cb + b) * 0x10001u;
+        *reinterpret_cast<uint4*>(out + p) = make_uint4(k2, k2, k2, k2);
+      } else {
+        uint32_t bb = b;
+        uint32_t k[4];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          while ((uint64_t)s_bs[bb + 1] <= p + e) ++bb;
+          const uint32_t ke = key_of(cb + bb);
+          if (e & 1) k[e >> 1] |= ke << 16;
+          else k[e >> 1] = ke;
+        }
+        *reinterpret_cast<uint4*>(out + p) = make_uint4(k[0], k[1], k[2], k[3]);
+      }
+    }
+    w0 = w1;
+    __syncthreads();  // s_w, s_bs reused
   }
 }
 
@@ -915,6 +1063,54 @@ struct LookbackTimer {
   }
 };
 
+// Routed pass: one owner's run of a tile -- tile positions [j0, j1), whose
+// E-byte elements sit in shared memory at src + j * SS -- to its destination
+// dst + j * E (dst may be a peer's memory).  16-byte stores on the aligned
+// body of the run, element stores on its head and tail.
+struct RoutedRun {
+  unsigned long long dk, dv;  // destination of tile position 0 (keys, values)
+  uint32_t j0, j1, tile, pad;
+};
+#ifndef CUSORT_ROUTED_VEC
+#define CUSORT_ROUTED_VEC 0
+#endif
+template <int E, int SS, int THREADS>
+__device__ __forceinline__ void routed_run_copy(const uint8_t* src, unsigned long long dst, uint32_t j0, uint32_t j1,
+                                                uint32_t tid) {
+  using T = typename dev::UIntOf<E>::T;
+  constexpr uint32_t P = 16 / E;
+  auto elem = [&](uint32_t j) { return *reinterpret_cast<const T*>(src + (size_t)j * SS); };
+  // first position at or after j0 whose destination is 16-byte aligned
+  const uint32_t mis = (uint32_t)((dst + (unsigned long long)j0 * E) & 15ull) / E;
+  const uint32_t ja = min(j1, j0 + (mis ? P - mis : 0u));
+  const uint32_t nv = (j1 - ja) / P, jt = ja + nv * P;
+  const uint32_t nh = ja - j0;
+  if (tid < nh) reinterpret_cast<T*>(dst)[j0 + tid] = elem(j0 + tid);
+  else if (tid - nh < j1 - jt) reinterpret_cast<T*>(dst)[jt + tid - nh] = elem(jt + tid - nh);
+#pragma unroll 1
+  for (uint32_t v = tid; v < nv; v += THREADS) {
+    const uint32_t j = ja + v * P;
+    uint4 w;
+    if constexpr (E == 16) {
+      w = elem(j);
+    } else if constexpr (E == 8) {
+      const unsigned long long e0 = elem(j), e1 = elem(j + 1);
+      w = make_uint4((uint32_t)e0, (uint32_t)(e0 >> 32), (uint32_t)e1, (uint32_t)(e1 >> 32));
+    } else {
+      uint32_t x[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int k = 0; k < (int)(4 / E); ++k) acc |= (uint32_t)elem(j + i * (4 / E) + k) << (8 * E * k);
+        x[i] = acc;
+      }
+      w = make_uint4(x[0], x[1], x[2], x[3]);
+    }
+    *reinterpret_cast<uint4*>(dst + (unsigned long long)j * E) = w;
+  }
+}
+
 template <class CFG>
 __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const typename CFG::Args a) {
   using K = typename dev::UIntOf<CFG::KB>::T;
@@ -1005,6 +1201,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       s_rptr[3 * kMaxRouteRanks + tid] = route->base[tid];
       s_rfirst[tid] = route->first_digit[tid];
       s_rfirst[kMaxRouteRanks + tid] = route->last_digit[tid];
+      reinterpret_cast<RoutedRun*>(smem + CFG::OFF_RDST)[tid].tile = ~0u;  // no run of any tile yet
     }
     __syncthreads();
   } else {
@@ -1294,15 +1491,34 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         const unsigned long long run = s_rptr[3 * kMaxRouteRanks + q] + earlier;
         const unsigned long long rel = run - (unsigned long long)s_tstart[lo];  // modulo 2^64
         const unsigned long long first = rel + s_tstart[tid];
-        unsigned long long dk = 0, dv = 0;
-        if (first + cnt <= s_rptr[2 * kMaxRouteRanks + q]) {
-          dk = s_rptr[q] + rel * sizeof(K);
-          if constexpr (HAS_V) dv = s_rptr[kMaxRouteRanks + q] + rel * sizeof(V);
-        } else if (cnt) {
-          atomicOr(a.status, kStatusRouteOverflow);
+        if constexpr (CUSORT_ROUTED_VEC) {
+          // one run per (tile, owner): its first digit's thread writes the
+          // start and the destinations, its last digit's thread the end (an
+          // owner without digits keeps a stale tile tag and is skipped)
+          RoutedRun* s_runs = reinterpret_cast<RoutedRun*>(smem + CFG::OFF_RDST);
+          if (tid == lo) {
+            s_runs[q].dk = s_rptr[q] + rel * sizeof(K);
+            s_runs[q].dv = HAS_V ? s_rptr[kMaxRouteRanks + q] + rel * sizeof(V) : 0ull;
+            s_runs[q].j0 = s_tstart[lo];
+            s_runs[q].tile = tile;
+          }
+          if (tid == hi) {
+            // a run that would not fit is dropped whole and flagged
+            const bool fits = first + cnt <= s_rptr[2 * kMaxRouteRanks + q];
+            if (!fits && s_tstart[tid] + cnt > s_tstart[lo]) atomicOr(a.status, kStatusRouteOverflow);
+            s_runs[q].j1 = fits ? s_tstart[tid] + cnt : s_tstart[lo];
+          }
+        } else {
+          unsigned long long dk = 0, dv = 0;
+          if (first + cnt <= s_rptr[2 * kMaxRouteRanks + q]) {
+            dk = s_rptr[q] + rel * sizeof(K);
+            if constexpr (HAS_V) dv = s_rptr[kMaxRouteRanks + q] + rel * sizeof(V);
+          } else if (cnt) {
+            atomicOr(a.status, kStatusRouteOverflow);
+          }
+          s_dst[tid] = dk;
+          s_dst[kRadix + tid] = dv;
         }
-        s_dst[tid] = dk;
-        s_dst[kRadix + tid] = dv;
       }
       __syncthreads();
     }
@@ -1340,7 +1556,23 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         if constexpr (HAS_V) vals_out[dst] = s_vsort[j];
       }
     };
-    if (valid == (uint32_t)TILE) {
+    if constexpr (CFG::ROUTED && CUSORT_ROUTED_VEC) {
+      // the tile is one contiguous run per owner: copy each with 16-byte stores
+      const RoutedRun* s_runs = reinterpret_cast<const RoutedRun*>(smem + CFG::OFF_RDST);
+      const uint8_t* ksrc = CFG::PACKED_KV ? reinterpret_cast<const uint8_t*>(s_kv)
+                                           : reinterpret_cast<const uint8_t*>(s_keys);
+      const uint8_t* vsrc = CFG::PACKED_KV ? reinterpret_cast<const uint8_t*>(s_kv) + 4
+                                           : reinterpret_cast<const uint8_t*>(s_vsort);
+      constexpr int KS = CFG::PACKED_KV ? 8 : CFG::KB;
+      constexpr int VS = CFG::PACKED_KV ? 8 : (HAS_V ? CFG::VB : 1);
+#pragma unroll 1
+      for (int q = 0; q < kMaxRouteRanks; ++q) {
+        const RoutedRun r = s_runs[q];
+        if (r.tile != tile || r.j1 <= r.j0) continue;
+        routed_run_copy<CFG::KB, KS, THREADS>(ksrc, r.dk, r.j0, r.j1, tid);
+        if constexpr (HAS_V) routed_run_copy<CFG::VB, VS, THREADS>(vsrc, r.dv, r.j0, r.j1, tid);
+      }
+    } else if (valid == (uint32_t)TILE) {
 #pragma unroll
       for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS);
     } else {

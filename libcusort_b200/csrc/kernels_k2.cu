@@ -13,6 +13,7 @@ bool get_fill16_kernels(int off_bytes, KernelInfo* hist, KernelInfo* fill) {
   hist->func = w ? reinterpret_cast<const void*>(&hist16_kernel<unsigned long long>)
                  : reinterpret_cast<const void*>(&hist16_kernel<unsigned int>);
   hist->threads = 1024;
+  hist->tile = kHist16Readers;  // CTAs that read each key
   hist->smem = (size_t)kBins16 / 2 * 4;
   fill->func = w ? reinterpret_cast<const void*>(&fill16_kernel<unsigned long long>)
                  : reinterpret_cast<const void*>(&fill16_kernel<unsigned int>);

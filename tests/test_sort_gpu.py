@@ -275,3 +275,22 @@ def test_short_keys_one_pass_few_values():
     keys = np.random.default_rng(1).choice(np.array([0, 1, 65535, 32768, 32767], dtype=np.uint16), size=n)
     check("u16", keys, None)
     check("i16", keys.view(np.int16), None, desc=True)
+
+
+@pytest.mark.parametrize("kt", ["u16", "i16"])
+def test_short_keys_one_pass_counter_overflow(kt):
+    # the 16-bit-digit count keeps two bins per 32-bit shared word (16-bit halves) and moves
+    # 0x8000 to the global count whenever a half reaches it: with 2^24 keys each of the ~148
+    # counting CTAs sees tens of thousands of copies of the heavy values, whose bins (0x1234,
+    # 0x1235) share one word, so both halves cross 0x8000 in every CTA without carrying into
+    # each other
+    n = (1 << 24) + 5
+    keys = D.uniform_bits(kt, n, seed=77)
+    heavy = np.array([0x1234, 0x1235], dtype=np.uint16).view(keys.dtype)
+    keys[: n * 2 // 5] = heavy[0]
+    keys[n * 2 // 5: n * 3 // 4] = heavy[1]
+    np.random.default_rng(78).shuffle(keys)
+    check(kt, keys, None)
+    check(kt, keys, None, desc=True)
+    same = np.full((1 << 23) + 1, heavy[0], dtype=keys.dtype)  # every key equal
+    check(kt, same, None)
