@@ -140,12 +140,24 @@ constexpr int fit_kpt() {
 
 // Routed partition pass (multi-GPU): CTAs per SM, tile size in percent of
 // the plain staged shape's, and whether the tile is fitted to the 32-bit
-// warp counters (tuning knobs).
+// warp counters.  One CTA per SM with 1.4x the items per thread (128
+// registers): measured on 2 B200s, 2^31 int32+uint32 pairs per GPU, routed
+// pass ms: two CTAs per SM, fitted (17 items per thread) 18.3, not fitted
+// (20 items, 16-bit counters; its tables overflowed the two-CTA share, so
+// one CTA per SM) 15.8, one CTA 20 / 28 / 36 items 15.7 / 15.5 / 15.5.
+// Writing each owner's run of a tile with 16-byte stores instead of one
+// item per thread measured 15.5 -> 15.7-18.9 ms, so the per-item scatter
+// stays: the pass is bound by the peer link, not by store instructions.
 #ifndef CUSORT_ROUTED_MINB
-#define CUSORT_ROUTED_MINB 2
+#define CUSORT_ROUTED_MINB 1
 #endif
 #ifndef CUSORT_ROUTED_KPT_PCT
-#define CUSORT_ROUTED_KPT_PCT 100
+#define CUSORT_ROUTED_KPT_PCT 140
+#endif
+// Items of fewer than 8 bytes keep the plain shape (two CTAs per SM): their
+// larger tiles spilled registers at one CTA per SM.
+#ifndef CUSORT_ROUTED_MIN_ITEM_BYTES
+#define CUSORT_ROUTED_MIN_ITEM_BYTES 8
 #endif
 #ifndef CUSORT_FIT_ROUTED
 #define CUSORT_FIT_ROUTED 1
@@ -154,8 +166,9 @@ constexpr int fit_kpt() {
 template <int KB, int VB, typename Off, bool FK, bool ROUTED = false, bool SEG = false>
 inline void fill_onesweep(KernelInfo* os) {
   using S = TileShape<KB, VB, ROUTED || SEG || (sizeof(Off) == 8 && !CUSORT_PIPE_WIDE_OFFSETS)>;
-  constexpr int MINB = ROUTED ? CUSORT_ROUTED_MINB : S::MINB;
-  constexpr int KPT0 = ROUTED ? S::KPT * CUSORT_ROUTED_KPT_PCT / 100 : S::KPT;
+  constexpr bool ROUTED_WIDE = ROUTED && KB + VB >= CUSORT_ROUTED_MIN_ITEM_BYTES;
+  constexpr int MINB = ROUTED_WIDE ? CUSORT_ROUTED_MINB : S::MINB;
+  constexpr int KPT0 = ROUTED_WIDE ? S::KPT * CUSORT_ROUTED_KPT_PCT / 100 : S::KPT;
   constexpr int KPT = (ROUTED && !CUSORT_FIT_ROUTED) ? KPT0 : fit_kpt<KB, VB, Off, S::THREADS, KPT0, MINB, FK, ROUTED, SEG>();
   using CFG = OnesweepCfg<KB, VB, Off, S::THREADS, KPT, MINB, FK, ROUTED, SEG>;
   if constexpr (CFG::PIPE) os->func = reinterpret_cast<const void*>(&onesweep_pipe_kernel<CFG>);

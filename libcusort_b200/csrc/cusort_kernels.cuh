@@ -811,6 +811,34 @@ struct RankSlots {
 #define CUSORT_PREFETCH 0
 #endif
 
+// Bank swizzle of the sorted tile in shared memory: sorted position p lives
+// at p ^ ((p >> 5) & 31), a permutation inside each aligned block of 32, so
+// 32 consecutive positions (the scatter's reads) stay conflict-free while
+// positions 32k apart -- the same rank in digit runs of equal length, which
+// a slot of sorted or evenly spread keys writes at once -- fall into
+// different banks instead of one.  1 = on.
+#ifndef CUSORT_TILE_SWIZZLE
+#define CUSORT_TILE_SWIZZLE 1
+#endif
+// Full tiles whose keys all share one digit skip the ranking and go out in
+// input order (the reference's per-tile short-circuit): 1 = on.
+#ifndef CUSORT_ONE_DIGIT_TILES
+#define CUSORT_ONE_DIGIT_TILES 1
+#endif
+__device__ __forceinline__ uint32_t tile_swz(uint32_t p) {
+  return CUSORT_TILE_SWIZZLE ? p ^ ((p >> 5) & 31u) : p;
+}
+// tile_swz(tid + i * THREADS) for the scatter's i-th item of thread tid
+template <int THREADS>
+__device__ __forceinline__ uint32_t tile_swz_at(uint32_t tid, uint32_t i) {
+  if constexpr (CUSORT_TILE_SWIZZLE && THREADS == 512) {
+    // (p >> 5) & 31 = warp + 16 (i & 1) with 16 warps: only the lane bits change
+    return (tid ^ (tid >> 5) ^ ((i & 1u) << 4)) + i * THREADS;
+  } else {
+    return tile_swz(tid + i * THREADS);
+  }
+}
+
 // Rank mode per key/value width (measured on B200, see OnesweepCfg).
 #ifndef CUSORT_KEYS_RANK_MODE
 #define CUSORT_KEYS_RANK_MODE 6
@@ -1063,54 +1091,6 @@ struct LookbackTimer {
   }
 };
 
-// Routed pass: one owner's run of a tile -- tile positions [j0, j1), whose
-// E-byte elements sit in shared memory at src + j * SS -- to its destination
-// dst + j * E (dst may be a peer's memory).  16-byte stores on the aligned
-// body of the run, element stores on its head and tail.
-struct RoutedRun {
-  unsigned long long dk, dv;  // destination of tile position 0 (keys, values)
-  uint32_t j0, j1, tile, pad;
-};
-#ifndef CUSORT_ROUTED_VEC
-#define CUSORT_ROUTED_VEC 0
-#endif
-template <int E, int SS, int THREADS>
-__device__ __forceinline__ void routed_run_copy(const uint8_t* src, unsigned long long dst, uint32_t j0, uint32_t j1,
-                                                uint32_t tid) {
-  using T = typename dev::UIntOf<E>::T;
-  constexpr uint32_t P = 16 / E;
-  auto elem = [&](uint32_t j) { return *reinterpret_cast<const T*>(src + (size_t)j * SS); };
-  // first position at or after j0 whose destination is 16-byte aligned
-  const uint32_t mis = (uint32_t)((dst + (unsigned long long)j0 * E) & 15ull) / E;
-  const uint32_t ja = min(j1, j0 + (mis ? P - mis : 0u));
-  const uint32_t nv = (j1 - ja) / P, jt = ja + nv * P;
-  const uint32_t nh = ja - j0;
-  if (tid < nh) reinterpret_cast<T*>(dst)[j0 + tid] = elem(j0 + tid);
-  else if (tid - nh < j1 - jt) reinterpret_cast<T*>(dst)[jt + tid - nh] = elem(jt + tid - nh);
-#pragma unroll 1
-  for (uint32_t v = tid; v < nv; v += THREADS) {
-    const uint32_t j = ja + v * P;
-    uint4 w;
-    if constexpr (E == 16) {
-      w = elem(j);
-    } else if constexpr (E == 8) {
-      const unsigned long long e0 = elem(j), e1 = elem(j + 1);
-      w = make_uint4((uint32_t)e0, (uint32_t)(e0 >> 32), (uint32_t)e1, (uint32_t)(e1 >> 32));
-    } else {
-      uint32_t x[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint32_t acc = 0;
-#pragma unroll
-        for (int k = 0; k < (int)(4 / E); ++k) acc |= (uint32_t)elem(j + i * (4 / E) + k) << (8 * E * k);
-        x[i] = acc;
-      }
-      w = make_uint4(x[0], x[1], x[2], x[3]);
-    }
-    *reinterpret_cast<uint4*>(dst + (unsigned long long)j * E) = w;
-  }
-}
-
 template <class CFG>
 __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const typename CFG::Args a) {
   using K = typename dev::UIntOf<CFG::KB>::T;
@@ -1201,7 +1181,6 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       s_rptr[3 * kMaxRouteRanks + tid] = route->base[tid];
       s_rfirst[tid] = route->first_digit[tid];
       s_rfirst[kMaxRouteRanks + tid] = route->last_digit[tid];
-      reinterpret_cast<RoutedRun*>(smem + CFG::OFF_RDST)[tid].tile = ~0u;  // no run of any tile yet
     }
     __syncthreads();
   } else {
@@ -1392,7 +1371,10 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       incl = dev::warp_inclusive_scan(cnt, lane);
       if (lane == 31) s_misc[4 + warp] = incl;
     }
-    __syncthreads();
+    // a full tile whose keys all share one digit is already in sorted order
+    // (plain passes: the tile then goes out from the registers, unranked)
+    constexpr bool PLAIN = CUSORT_ONE_DIGIT_TILES && !CFG::ROUTED && !CFG::SEG;
+    const bool one_digit = __syncthreads_or(PLAIN && tid < kRadix && cnt == (uint32_t)TILE) != 0;
     if (tid < kRadix) {
       uint32_t pre = 0;
       for (uint32_t w = 0; w < warp; ++w) pre += s_misc[4 + w];
@@ -1409,6 +1391,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         // rank against the per-warp position counters, store at once
         auto store = [&](auto sc, uint32_t pos) {
           constexpr int S = decltype(sc)::value;
+          pos = tile_swz(pos);
           if constexpr (CFG::PACKED_KV) {
             s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
           } else {
@@ -1425,7 +1408,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       } else {
 #pragma unroll
         for (int s = 0; s < KPT; ++s) {
-          const uint32_t pos = WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8);
+          const uint32_t pos = tile_swz(WC::get(s_wtab, warp, dr[s] & 0xffu) + (dr[s] >> 8));
           if constexpr (CFG::PACKED_KV) {
             s_kv[pos] = make_uint2((uint32_t)key[s], (uint32_t)val[s]);
           } else {
@@ -1462,6 +1445,34 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
     }
+    if (PLAIN && one_digit) {
+      __syncthreads();
+      if constexpr (TIMED) {
+        if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
+      }
+      if constexpr (CFG::DIRECT_LOAD) {
+        const Off dst = s_goff[kdigit(key[0])] + (Off)(wfirst_c + lane);
+#pragma unroll
+        for (int s = 0; s < KPT; ++s) {
+          keys_out[dst + (Off)(s * 32)] = key[s];
+          if constexpr (VREG) vals_out[dst + (Off)(s * 32)] = val[s];
+        }
+      } else {
+        // from the staged copy of the tile, which the reorder has not touched
+        const Off dst = s_goff[kdigit(s_keys[0])];
+#pragma unroll 4
+        for (uint32_t j = tid; j < (uint32_t)TILE; j += THREADS) {
+          keys_out[dst + (Off)j] = s_keys[j];
+          if constexpr (HAS_V) vals_out[dst + (Off)j] = s_vals[j];
+        }
+      }
+      dev::fence_proxy_async_smem();  // before the buffer is refilled by TMA
+      if constexpr (CFG::PREFETCH) {
+        cur = nxt;
+        if (NBUF == 2) b ^= 1;
+      }
+      continue;
+    }
     reorder();
     __syncthreads();
     if constexpr (TIMED) {
@@ -1491,50 +1502,32 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         const unsigned long long run = s_rptr[3 * kMaxRouteRanks + q] + earlier;
         const unsigned long long rel = run - (unsigned long long)s_tstart[lo];  // modulo 2^64
         const unsigned long long first = rel + s_tstart[tid];
-        if constexpr (CUSORT_ROUTED_VEC) {
-          // one run per (tile, owner): its first digit's thread writes the
-          // start and the destinations, its last digit's thread the end (an
-          // owner without digits keeps a stale tile tag and is skipped)
-          RoutedRun* s_runs = reinterpret_cast<RoutedRun*>(smem + CFG::OFF_RDST);
-          if (tid == lo) {
-            s_runs[q].dk = s_rptr[q] + rel * sizeof(K);
-            s_runs[q].dv = HAS_V ? s_rptr[kMaxRouteRanks + q] + rel * sizeof(V) : 0ull;
-            s_runs[q].j0 = s_tstart[lo];
-            s_runs[q].tile = tile;
-          }
-          if (tid == hi) {
-            // a run that would not fit is dropped whole and flagged
-            const bool fits = first + cnt <= s_rptr[2 * kMaxRouteRanks + q];
-            if (!fits && s_tstart[tid] + cnt > s_tstart[lo]) atomicOr(a.status, kStatusRouteOverflow);
-            s_runs[q].j1 = fits ? s_tstart[tid] + cnt : s_tstart[lo];
-          }
-        } else {
-          unsigned long long dk = 0, dv = 0;
-          if (first + cnt <= s_rptr[2 * kMaxRouteRanks + q]) {
-            dk = s_rptr[q] + rel * sizeof(K);
-            if constexpr (HAS_V) dv = s_rptr[kMaxRouteRanks + q] + rel * sizeof(V);
-          } else if (cnt) {
-            atomicOr(a.status, kStatusRouteOverflow);
-          }
-          s_dst[tid] = dk;
-          s_dst[kRadix + tid] = dv;
+        unsigned long long dk = 0, dv = 0;
+        if (first + cnt <= s_rptr[2 * kMaxRouteRanks + q]) {
+          dk = s_rptr[q] + rel * sizeof(K);
+          if constexpr (HAS_V) dv = s_rptr[kMaxRouteRanks + q] + rel * sizeof(V);
+        } else if (cnt) {
+          atomicOr(a.status, kStatusRouteOverflow);
         }
+        s_dst[tid] = dk;
+        s_dst[kRadix + tid] = dv;
       }
       __syncthreads();
     }
 
     // ---- 6. coalesced scatter
-    auto put_one = [&](uint32_t j) {
+    // sorted position j, read from its swizzled slot p
+    auto put_one = [&](uint32_t j, uint32_t p) {
       if constexpr (CFG::ROUTED) {
         K k;
         V v;
         if constexpr (CFG::PACKED_KV) {
-          const uint2 kv = s_kv[j];
+          const uint2 kv = s_kv[p];
           k = (K)kv.x;
           v = (V)kv.y;
         } else {
-          k = s_keys[j];
-          if constexpr (HAS_V) v = s_vsort[j];
+          k = s_keys[p];
+          if constexpr (HAS_V) v = s_vsort[p];
         }
         const unsigned long long* s_dst = reinterpret_cast<const unsigned long long*>(smem + CFG::OFF_RDST);
         const uint32_t d = dev::digit_k<CFG::FLOAT_KEY, K>(k, tc, tf, a.shift, a.mask);
@@ -1544,39 +1537,23 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
           if constexpr (HAS_V) reinterpret_cast<V*>(s_dst[kRadix + d])[j] = v;
         }
       } else if constexpr (CFG::PACKED_KV) {
-        const uint2 kv = s_kv[j];
+        const uint2 kv = s_kv[p];
         const K k = (K)kv.x;
         const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
         vals_out[dst] = (V)kv.y;
       } else {
-        const K k = s_keys[j];
+        const K k = s_keys[p];
         const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
-        if constexpr (HAS_V) vals_out[dst] = s_vsort[j];
+        if constexpr (HAS_V) vals_out[dst] = s_vsort[p];
       }
     };
-    if constexpr (CFG::ROUTED && CUSORT_ROUTED_VEC) {
-      // the tile is one contiguous run per owner: copy each with 16-byte stores
-      const RoutedRun* s_runs = reinterpret_cast<const RoutedRun*>(smem + CFG::OFF_RDST);
-      const uint8_t* ksrc = CFG::PACKED_KV ? reinterpret_cast<const uint8_t*>(s_kv)
-                                           : reinterpret_cast<const uint8_t*>(s_keys);
-      const uint8_t* vsrc = CFG::PACKED_KV ? reinterpret_cast<const uint8_t*>(s_kv) + 4
-                                           : reinterpret_cast<const uint8_t*>(s_vsort);
-      constexpr int KS = CFG::PACKED_KV ? 8 : CFG::KB;
-      constexpr int VS = CFG::PACKED_KV ? 8 : (HAS_V ? CFG::VB : 1);
-#pragma unroll 1
-      for (int q = 0; q < kMaxRouteRanks; ++q) {
-        const RoutedRun r = s_runs[q];
-        if (r.tile != tile || r.j1 <= r.j0) continue;
-        routed_run_copy<CFG::KB, KS, THREADS>(ksrc, r.dk, r.j0, r.j1, tid);
-        if constexpr (HAS_V) routed_run_copy<CFG::VB, VS, THREADS>(vsrc, r.dv, r.j0, r.j1, tid);
-      }
-    } else if (valid == (uint32_t)TILE) {
+    if (valid == (uint32_t)TILE) {
 #pragma unroll
-      for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS);
+      for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS, tile_swz_at<THREADS>(tid, i));
     } else {
-      for (uint32_t j = tid; j < valid; j += THREADS) put_one(j);
+      for (uint32_t j = tid; j < valid; j += THREADS) put_one(j, tile_swz(j));
     }
     dev::fence_proxy_async_smem();  // before the buffer is refilled by TMA
     if constexpr (CFG::PREFETCH) {
@@ -1740,7 +1717,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
       incl = dev::warp_inclusive_scan(cnt, lane);
       if (lane == 31) s_misc[4 + warp] = incl;
     }
-    __syncthreads();
+    // a full tile whose keys all share one digit is already in sorted order
+    const bool one_digit =
+        __syncthreads_or(CUSORT_ONE_DIGIT_TILES && tid < kRadix && cnt == (uint32_t)TILE) != 0;
     if (tid < kRadix) {
       uint32_t pre = 0;
       for (uint32_t w = 0; w < warp; ++w) pre += s_misc[4 + w];
@@ -1770,9 +1749,27 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
         s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
     }
+    if (one_digit) {
+      // no ranking: the tile goes out from the registers in input order
+      if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
+      __syncthreads();
+      if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
+      const Off dst = s_goff[kdigit(key[0])] + (Off)(wfirst + lane);
+#pragma unroll
+      for (int s = 0; s < KPT; ++s) {
+        keys_out[dst + (Off)(s * 32)] = key[s];
+        if constexpr (HAS_V) vals_out[dst + (Off)(s * 32)] = val[s];
+      }
+      const uint32_t nxt = s_misc[1];
+      if (nxt < num_tiles) load_tile(nxt);
+      WC::zero(s_wtab, warp, lane);
+      cur = nxt;
+      continue;
+    }
     {
       auto store = [&](auto sc, uint32_t pos) {
         constexpr int S = decltype(sc)::value;
+        pos = tile_swz(pos);
         if constexpr (CFG::PACKED_KV) {
           s_kv[pos] = make_uint2((uint32_t)key[S], (uint32_t)val[S]);
         } else {
@@ -1796,26 +1793,27 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     WC::zero(s_wtab, warp, lane);  // this warp's table: its ranking is done
 
     // ---- coalesced scatter
-    auto put_one = [&](uint32_t j) {
+    // sorted position j, read from its swizzled slot p
+    auto put_one = [&](uint32_t j, uint32_t p) {
       if constexpr (CFG::PACKED_KV) {
-        const uint2 kv = s_kv[j];
+        const uint2 kv = s_kv[p];
         const K k = (K)kv.x;
         const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
         vals_out[dst] = (V)kv.y;
       } else {
-        const K k = s_keys[j];
+        const K k = s_keys[p];
         const Off dst = s_goff[kdigit(k)] + (Off)j;
         keys_out[dst] = k;
-        if constexpr (HAS_V) vals_out[dst] = s_vals[j];
+        if constexpr (HAS_V) vals_out[dst] = s_vals[p];
       }
     };
     if (valid == (uint32_t)TILE) {
       constexpr int SU = CUSORT_PIPE_SCATTER_UNROLL;
 #pragma unroll SU
-      for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS);
+      for (int i = 0; i < KPT; ++i) put_one(tid + i * THREADS, tile_swz_at<THREADS>(tid, i));
     } else {
-      for (uint32_t j = tid; j < valid; j += THREADS) put_one(j);
+      for (uint32_t j = tid; j < valid; j += THREADS) put_one(j, tile_swz(j));
     }
     cur = nxt;
   }

@@ -294,3 +294,18 @@ def test_short_keys_one_pass_counter_overflow(kt):
     check(kt, keys, None, desc=True)
     same = np.full((1 << 23) + 1, heavy[0], dtype=keys.dtype)  # every key equal
     check(kt, same, None)
+
+
+@pytest.mark.parametrize("kt,vb", [("u32", 0), ("i32", 4), ("f32", 0), ("u64", 8), ("f64", 0), ("u16", 2), ("u8", 4),
+                                   ("i64", 16)])
+@pytest.mark.parametrize("desc", [False, True])
+def test_one_digit_tiles(kt, vb, desc):
+    # runs of 2^15 equal keys: whole tiles whose keys share their digit in every pass skip the
+    # ranking and go out in input order; the tiles that straddle two runs are ranked as usual
+    n = (1 << 21) + 12_345
+    table = D.uniform_bits(kt, (n >> 15) + 1, seed=91)
+    keys = table[np.arange(n) >> 15]
+    vals = D.values_for(n, vb) if vb else None
+    check(kt, keys, vals, desc=desc)
+    if vb:
+        check(kt, keys, vals, desc=desc, api="db")
