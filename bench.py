@@ -22,7 +22,9 @@ one complete sort call (init + histogram + 4 onesweep passes).
 secondary  u32 keys-only 2^26; the other BASELINE.json single-GPU configs at
             2^26; configs[0] (2^20 u32 keys-only, 4 MiB: L2-resident, so a
             hot-L2, launch-latency-bound figure), direct and graph launches;
-            ours only: segmented sort of 2^26 pairs, one entry per length class
+            input orders (sorted, reverse sorted, all equal, 16 distinct
+            values; keys-only and pairs); ours only: segmented sort of 2^26
+            pairs, one entry per length class
 
 N>1 (torchrun): sharded multi-GPU sort of 2^32 int32/uint32 pairs split over
 the GPUs (strong scaling, configs[4]); --weak for 2^26 pairs per GPU.
@@ -440,6 +442,7 @@ def run_single(args, torch, dist=None, rank=0, world=1):
         out["secondary"]["double_buffer_api_2^26"] = double_buffer_forms(args, torch, device)
         out["secondary"]["other_configs_2^26"] = other_configs(args, torch, device)
         out["secondary"]["configs[0]_u32_keys_2^20_hot_l2"] = small_hot_l2(args, torch, device)
+        out["secondary"]["input_patterns_2^26"] = input_patterns(args, torch, device)
         if args.impl == "ours":
             out["secondary"]["segmented_2^26"] = segmented(args, torch, device)
     if args.impl == "ours" and not args.no_cpu_baseline:
@@ -705,6 +708,40 @@ def other_configs(args, torch, device):
     draws = torch.multinomial((ranks ** -1.1).float(), n, replacement=True, generator=g)
     run("configs[3]_u32_keys_bits_0_20_zipf_u32_values", "u32", 4, 4, table[draws],
         torch.arange(n, dtype=torch.int32, device=device), 4, begin=0, end=20)
+    return res
+
+
+def input_patterns(args, torch, device):
+    """int32 keys-only and int32 + uint32 index pairs at 2^26 in orders and cardinalities a
+    uniform bench does not show, same impl and API (in/out pointers): already sorted (keys =
+    63 i), reverse sorted, all keys equal, 16 distinct values in random order.  Time per sort
+    (CUDA events, 3 warm-up + 10)."""
+    n = 1 << args.log2n
+    g = torch.Generator(device=device)
+    g.manual_seed(12)
+    stream = torch.cuda.current_stream().cuda_stream
+    i = torch.arange(n, dtype=torch.int64, device=device)
+    vals = i.to(torch.int32).view(torch.uint8)
+    dummy = torch.empty(1, dtype=torch.uint8, device=device)
+    pats = {
+        "sorted": lambda: (i * 63).to(torch.int32),
+        "reverse_sorted": lambda: ((n - i) * 63).to(torch.int32),
+        "all_equal": lambda: torch.full((n,), 123456789, dtype=torch.int32, device=device),
+        "16_distinct_values": lambda: (torch.randint(0, 16, (n,), device=device, generator=g) * 0x10204081).to(
+            torch.int32),
+    }
+    res = {}
+    for name, make in pats.items():
+        kin = make().contiguous().view(torch.uint8)
+        kout = torch.empty_like(kin)
+        for vb in (0, 4):
+            vout = torch.empty_like(vals) if vb else dummy
+            srt = Sorter(args.impl, torch, "i32", 5, 4, vb, n, kin, kout, vals if vb else dummy, vout, stream)
+            ms = time_steps(torch, srt, 10, 3) / 10
+            res[f"{name}_{'i32_u32_pairs' if vb else 'i32_keys'}"] = {"ms_per_step": round(ms, 4),
+                                                                     "gkeys_per_s": round(n / (ms * 1e-3) / 1e9, 2)}
+            del srt, vout
+        del kin, kout
     return res
 
 
