@@ -183,11 +183,10 @@ __global__ void __launch_bounds__(256) fill_bytes_kernel(const FillArgs a) {
 // schedule: equal digits are equal keys, so counting is sorting).
 //   hist16_kernel: one 1024-thread CTA per SM counts its share of the keys
 //     (16-byte loads, four in flight per thread) into all 65536 bins held as
-//     packed 16-bit counters (two bins per shared word, 128 KB).  The add
-//     that takes a half from 0x7fff to 0x8000 -- the only add that flips
-//     that half's top bit, since the half is brought back below 0x8000 right
-//     after -- moves 0x8000 of it to the global count, so a counter never
-//     carries into its neighbour.  At the end one global atomic per nonzero
+//     packed 16-bit counters (two bins per shared word, 128 KB).  An add
+//     that flips bit 14 of its half moves 0x4000 of the half to the global
+//     count, so a counter never carries into its neighbour (see count_vec).
+//     At the end one global atomic per nonzero
 //     bin and one per nonzero group of 256 bins.  (CUSORT_HIST16_PACKED=0:
 //     32-bit counters, CTA pairs splitting the bins, every key read by both
 //     CTAs of a pair.)
@@ -224,16 +223,16 @@ __global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
   __syncthreads();
   const uint16_t* keys = static_cast<const uint16_t*>(a.keys);
   const uint32_t xc = a.xor_c & 0xffffu;
-  // m (< 0x8000) more copies of key k
+  // m (<= 0x4000) more copies of key k
   auto count_m = [&](uint32_t k, uint32_t m) {
     const uint32_t t = (k ^ xc) & 0xffffu;
     if constexpr (PACKED) {
       const uint32_t sh = (t & 1u) << 4, inc = m << sh;
       const uint32_t old = atomicAdd(s_cnt16 + (t >> 1), inc);
-      if ((old ^ (old + inc)) & 0x80008000u) {
-        atomicSub(s_cnt16 + (t >> 1), 0x8000u << sh);
-        atomicAdd(g + t, (Off)0x8000u);
-        atomicAdd(gg + (t >> 8), (Off)0x8000u);
+      if ((old ^ (old + inc)) & 0x40004000u) {
+        atomicSub(s_cnt16 + (t >> 1), 0x4000u << sh);
+        atomicAdd(g + t, (Off)0x4000u);
+        atomicAdd(gg + (t >> 8), (Off)0x4000u);
       }
     } else {
       if ((t >> 15) == half) atomicAdd(s_cnt16 + (t & 0x7fffu), m);
@@ -248,10 +247,34 @@ __global__ void __launch_bounds__(1024, 1) hist16_kernel(const Fill16Args a) {
   const uint64_t stride = (uint64_t)parts * 1024;
   auto count_vec = [&](const uint4& x) {
     const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+    if constexpr (PACKED) {
+      // the 8 adds first (8 atomics in flight), then the 8 tests: an add that
+      // flipped bit 14 of its half moves 0x4000 of the half to the global
+      // count.  Every such move follows an add that took the half to 0x4000
+      // or more, so the half never borrows; and until the move lands the half
+      // can take another 0xbfff adds before it would carry into its
+      // neighbour -- far more than the 8 per thread that are in flight here
+      uint32_t t[8], sh[8], old[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      count(w[e] & 0xffffu);
-      count(w[e] >> 16);
+      for (int e = 0; e < 8; ++e) {
+        t[e] = ((e & 1 ? w[e >> 1] >> 16 : w[e >> 1]) ^ xc) & 0xffffu;
+        sh[e] = (t[e] & 1u) << 4;
+        old[e] = atomicAdd(s_cnt16 + (t[e] >> 1), 1u << sh[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if ((old[e] ^ (old[e] + (1u << sh[e]))) & 0x40004000u) {
+          atomicSub(s_cnt16 + (t[e] >> 1), 0x4000u << sh[e]);
+          atomicAdd(g + t[e], (Off)0x4000u);
+          atomicAdd(gg + (t[e] >> 8), (Off)0x4000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        count(w[e] & 0xffffu);
+        count(w[e] >> 16);
+      }
     }
   };
   // four independent 16-byte loads in flight per thread (one CTA of 1024
