@@ -714,7 +714,8 @@ def other_configs(args, torch, device):
 def input_patterns(args, torch, device):
     """int32 keys-only and int32 + uint32 index pairs at 2^26 in orders and cardinalities a
     uniform bench does not show, same impl and API (in/out pointers): already sorted (keys =
-    63 i), reverse sorted, all keys equal, 16 distinct values in random order.  Time per sort
+    63 i), sorted with runs of 1024 equal keys (i >> 10), reverse sorted, all keys equal, 16
+    distinct values in random order.  Time per sort
     (CUDA events, 3 warm-up + 10)."""
     n = 1 << args.log2n
     g = torch.Generator(device=device)
@@ -725,6 +726,7 @@ def input_patterns(args, torch, device):
     dummy = torch.empty(1, dtype=torch.uint8, device=device)
     pats = {
         "sorted": lambda: (i * 63).to(torch.int32),
+        "sorted_runs_of_1024_equal": lambda: (i >> 10).to(torch.int32),
         "reverse_sorted": lambda: ((n - i) * 63).to(torch.int32),
         "all_equal": lambda: torch.full((n,), 123456789, dtype=torch.int32, device=device),
         "16_distinct_values": lambda: (torch.randint(0, 16, (n,), device=device, generator=g) * 0x10204081).to(

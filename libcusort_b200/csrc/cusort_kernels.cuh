@@ -848,6 +848,19 @@ struct RankSlots {
 #ifndef CUSORT_ONE_DIGIT_TILES
 #define CUSORT_ONE_DIGIT_TILES 1
 #endif
+// Full tiles whose digits never decrease in input order (sorted input, runs
+// of equal keys) are already in stable digit order: they skip the ranking
+// too.  The whole-tile check runs only when every warp's first and last
+// slots are non-decreasing across their lanes (a few instructions per warp
+// and tile).  1 = on.
+#ifndef CUSORT_SORTED_TILES
+#define CUSORT_SORTED_TILES 1
+#endif
+// this warp's 32 values non-decreasing from lane 0 to lane 31
+__device__ __forceinline__ bool warp_nondecreasing(uint32_t d, uint32_t lane) {
+  const uint32_t p = __shfl_up_sync(0xffffffffu, d, 1);
+  return __ballot_sync(0xffffffffu, lane != 0u && p > d) == 0u;
+}
 __device__ __forceinline__ uint32_t tile_swz(uint32_t p) {
   return CUSORT_TILE_SWIZZLE ? p ^ ((p >> 5) & 31u) : p;
 }
@@ -1365,6 +1378,14 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
     }
     uint2* s_kv = reinterpret_cast<uint2*>(s_keys);  // PACKED_KV view of the same buffer
     constexpr bool EARLY = CFG::RANK_MODE >= 4;
+    // sorted-tile check (see the pipelined pass): plain passes, staged tiles
+    constexpr bool SORTED = CUSORT_SORTED_TILES && CFG::RANK_MODE == 6 && !CFG::ROUTED && !CFG::SEG &&
+                            !CFG::DIRECT_LOAD;
+    bool hint = false;
+    if constexpr (SORTED) {
+      hint = warp_nondecreasing(RECOMP ? digit_at(0) : dr[0], lane) &&
+             warp_nondecreasing(RECOMP ? digit_at(KPT - 1) : dr[KPT - 1], lane);
+    }
     if constexpr (EARLY) {
 #pragma unroll
       for (int s = 0; s < KPT; ++s) WC::count_key(s_wtab, warp, RECOMP ? digit_at(s) : dr[s]);
@@ -1373,7 +1394,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       uint32_t prev = 0;
       RankSlots<CFG::RANK_MODE, 0, KPT>::run(s_wtab, warp, dr, lane, lt, prev);
     }
-    __syncthreads();
+    const bool all_hint = __syncthreads_and(hint) != 0;
 
     // ---- 3. per-digit counts, aggregate publish, tile-local digit offsets
     uint32_t cnt = 0;
@@ -1407,6 +1428,14 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
       for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
     }
     __syncthreads();
+    // a tile whose digits never decrease in input order: no ranking either
+    bool sorted_tile = false;
+    if (SORTED && all_hint && !one_digit && valid == (uint32_t)TILE) {
+      // neighbours compared in the staged tile (input order)
+      bool ok = true;
+      for (uint32_t j = tid + 1; j < (uint32_t)TILE; j += THREADS) ok = ok && kdigit(s_keys[j - 1]) <= kdigit(s_keys[j]);
+      sorted_tile = __syncthreads_and(ok) != 0;
+    }
 
     // ---- 4. reorder in shared memory (tile sorted by digit, stable)
     auto reorder = [&]() {
@@ -1468,13 +1497,13 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
     }
-    if (PLAIN && one_digit) {
+    if (PLAIN && (one_digit || sorted_tile)) {
       __syncthreads();
       if constexpr (TIMED) {
         if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
       }
       if constexpr (CFG::DIRECT_LOAD) {
-        const Off dst = s_goff[kdigit(key[0])] + (Off)(wfirst_c + lane);
+        const Off dst = s_goff[kdigit(key[0])] + (Off)(wfirst_c + lane);  // one digit only
 #pragma unroll
         for (int s = 0; s < KPT; ++s) {
           keys_out[dst + (Off)(s * 32)] = key[s];
@@ -1482,11 +1511,12 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_kernel(const
         }
       } else {
         // from the staged copy of the tile, which the reorder has not touched
-        const Off dst = s_goff[kdigit(s_keys[0])];
 #pragma unroll 4
         for (uint32_t j = tid; j < (uint32_t)TILE; j += THREADS) {
-          keys_out[dst + (Off)j] = s_keys[j];
-          if constexpr (HAS_V) vals_out[dst + (Off)j] = s_vals[j];
+          const K k = s_keys[j];
+          const Off dst = s_goff[kdigit(k)] + (Off)j;
+          keys_out[dst] = k;
+          if constexpr (HAS_V) vals_out[dst] = s_vals[j];
         }
       }
       dev::fence_proxy_async_smem();  // before the buffer is refilled by TMA
@@ -1643,6 +1673,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
   constexpr int THREADS = CFG::THREADS, KPT = CFG::KPT, TILE = CFG::TILE, WARPS = CFG::WARPS;
   constexpr bool HAS_V = CFG::VB > 0;
   static_assert(CFG::PIPE && CFG::RANK_MODE >= 4, "pipelined pass: early-count rank modes only");
+  constexpr bool SORTED = CUSORT_SORTED_TILES && CFG::RANK_MODE == 6;
 
   extern __shared__ __align__(128) uint8_t smem[];
   K* s_keys = reinterpret_cast<K*>(smem);  // the tile in sorted order
@@ -1716,10 +1747,15 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
     // ---- counting pre-pass (per-warp digit counts).  The digit is taken from
     // an opaque copy of the key: otherwise the compiler keeps every slot's
     // digit live until the ranking recomputes it, and spills registers.
+    bool hint = false;  // this warp's first and last slots non-decreasing (sorted-tile check)
+    if constexpr (SORTED) {
+      hint = warp_nondecreasing(kdigit(dev::opaque(key[0])), lane) &&
+             warp_nondecreasing(kdigit(dev::opaque(key[KPT - 1])), lane);
+    }
 #pragma unroll
     for (int s = 0; s < KPT; ++s)
       WC::count_key(s_wtab, warp, kdigit(dev::opaque(key[s])));
-    __syncthreads();
+    const bool all_hint = __syncthreads_and(hint) != 0;
 
     // ---- per-digit counts, aggregate publish, tile-local digit offsets
     uint32_t cnt = 0;
@@ -1752,6 +1788,25 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
       for (int w = 0; w < WARPS; ++w) WC::put(s_wtab, w, tid, WC::get(s_wtab, w, tid) + ts);
     }
     __syncthreads();
+    // a tile whose digits never decrease in input order: no ranking either
+    bool sorted_tile = false;
+    if (SORTED && all_hint && !one_digit && valid == (uint32_t)TILE) {
+      bool ok = true;
+      uint32_t last = 0;  // previous slot's lane-31 digit
+      static_for<0, KPT>([&](auto sc) {
+        constexpr int S = decltype(sc)::value;
+        const uint32_t d = digit(S);
+        ok = ok && warp_nondecreasing(d, lane) && (S == 0 || __shfl_sync(0xffffffffu, d, 0) >= last);
+        last = __shfl_sync(0xffffffffu, d, 31);
+      });
+      // warp edges through the (still unused) sorted-tile buffer
+      uint32_t* s_edge = reinterpret_cast<uint32_t*>(s_keys);
+      if (lane == 0) s_edge[warp] = digit(0);
+      if (lane == 31) s_edge[WARPS + warp] = digit(KPT - 1);
+      __syncthreads();
+      ok = ok && (warp == 0 || s_edge[WARPS + warp - 1] <= s_edge[warp]);
+      sorted_tile = __syncthreads_and(ok) != 0;
+    }
 
     // ---- decoupled lookback and rank + reorder: the digit-owning warps look
     // back first, so their L2 round trips overlap the other warps' reordering
@@ -1772,16 +1827,16 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::MINB) onesweep_pipe_kernel(
         s_goff[tid] = s_gbase[tid] + excl - (Off)s_tstart[tid];
       }
     }
-    if (one_digit) {
+    if (one_digit || sorted_tile) {
       // no ranking: the tile goes out from the registers in input order
       if (tid == 0) s_misc[1] = atomicAdd(a.tile_counter, 1u);
       __syncthreads();
       if (tid == 0) lbt.tile_done(s_misc + 14, a.status);
-      const Off dst = s_goff[kdigit(key[0])] + (Off)(wfirst + lane);
 #pragma unroll
       for (int s = 0; s < KPT; ++s) {
-        keys_out[dst + (Off)(s * 32)] = key[s];
-        if constexpr (HAS_V) vals_out[dst + (Off)(s * 32)] = val[s];
+        const Off dst = s_goff[kdigit(key[s])] + (Off)(wfirst + s * 32 + lane);
+        keys_out[dst] = key[s];
+        if constexpr (HAS_V) vals_out[dst] = val[s];
       }
       const uint32_t nxt = s_misc[1];
       if (nxt < num_tiles) load_tile(nxt);
