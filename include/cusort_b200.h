@@ -128,6 +128,23 @@ cudaError_t cusort_sort_pairs_wide(void* d_temp_storage, size_t* temp_storage_by
                                    const void* d_values_in, void* d_values_out, int64_t num_items, int begin_bit,
                                    int end_bit, int descending, cudaStream_t stream);
 
+/* ---- pairs held in host memory ---------------------------------------
+ * No counterpart in the reference (which sorts device memory only).  Sorts
+ * (keys, values) that live in HOST memory: h_keys_in / h_values_in are read,
+ * h_keys_out / h_values_out written (page-locked memory lets the copies run
+ * asynchronously and overlap).  The keys go up first and are sorted with their
+ * 32-bit input positions while the values go up; the sorted keys come down
+ * while the values are gathered through those positions, then the values come
+ * down.  Same ordering, stability and bit-range semantics as
+ * cusort_sort_pairs[_descending]; value_bytes 1, 2, 4, 8 or 16; num_items <
+ * 2^32.  d_temp_storage is DEVICE memory (two-phase size query as elsewhere).
+ * All work is ordered on `stream`: synchronise it before reading the host
+ * outputs. */
+cudaError_t cusort_sort_pairs_host(void* d_temp_storage, size_t* temp_storage_bytes, cusort_key_type key_type,
+                                   const void* h_keys_in, void* h_keys_out, size_t value_bytes,
+                                   const void* h_values_in, void* h_values_out, int64_t num_items, int begin_bit,
+                                   int end_bit, int descending, cudaStream_t stream);
+
 /* ---- sorting without any device allocation ----------------------------
  * No counterpart in the reference (which always takes temp storage from the
  * caller).  For callers that cannot allocate device memory when they need to

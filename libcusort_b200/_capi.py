@@ -43,6 +43,7 @@ SIGNATURES = {
     "cusort_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_descending": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _vp]),
     "cusort_sort_pairs_wide": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _i, _vp]),
+    "cusort_sort_pairs_host": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i, _i, _i, _vp]),
     "cusort_segmented_sort_keys": (_i, [_vp, _P_SZ, _i, _vp, _vp, _i64, _i64, _vp, _vp, _i, _i, _i, _vp]),
     "cusort_segmented_sort_pairs": (_i, [_vp, _P_SZ, _i, _vp, _vp, _sz, _vp, _vp, _i64, _i64, _vp, _vp, _i, _i, _i,
                                          _vp]),

@@ -190,3 +190,13 @@ def test_short_keys_one_digit_temp():
     # with values, too
     rc, nb = _query_pairs(2, 2, n, 0, 16)
     assert rc == 0 and nb > n * 4
+
+
+def test_host_pairs_rejects_bad_arguments():
+    # cusort_sort_pairs_host: value widths other than 1/2/4/8/16 and 2^32 items or more are refused
+    lib = _capi.load()
+    nb = C.c_size_t(0)
+    assert lib.cusort_sort_pairs_host(None, C.byref(nb), 4, None, None, 3, None, None, 10, 0, 32, 0, None) != 0
+    assert lib.cusort_sort_pairs_host(None, C.byref(nb), 4, None, None, 4, None, None, 1 << 32, 0, 32, 0, None) != 0
+    assert lib.cusort_sort_pairs_host(None, C.byref(nb), 4, None, None, 4, None, None, 1000, 0, 32, 0, None) == 0
+    assert nb.value > 1000 * (4 + 4) * 2
