@@ -156,6 +156,44 @@ def radix_sort(keys: torch.Tensor, values: torch.Tensor | None = None, *, descen
     return out_keys, (out_values if vb else None)
 
 
+def radix_sort_host(keys: torch.Tensor, values: torch.Tensor, *, descending: bool = False, begin_bit: int = 0,
+                    end_bit: int | None = None, device: torch.device | int | None = None):
+    """Stable sort of (keys, values) held in HOST memory on a GPU (cusort_sort_pairs_host): the
+    copies to and from the device overlap the sort and each other.  keys: contiguous 1-D CPU
+    tensor; values: CPU tensor with one row of 1, 2, 4, 8 or 16 bytes per key (pinned memory is
+    what lets the copies overlap).  Returns new pinned CPU tensors (sorted_keys, sorted_values),
+    complete when the call returns.  No CPU fallback: it needs the library and a CUDA device."""
+    if keys.device.type != "cpu" or values.device.type != "cpu":
+        raise ValueError("radix_sort_host takes CPU tensors; use radix_sort for CUDA tensors")
+    vb = _check_args(keys, values, None, None, None)
+    lib = _capi.load()
+    kt = key_type_of(keys.dtype)
+    n = keys.numel()
+    end_bit = 8 * keys.element_size() if end_bit is None else end_bit
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    kid = _capi.key_type_id(kt)
+    out_keys = torch.empty(keys.shape, dtype=keys.dtype, pin_memory=True)
+    out_values = torch.empty(values.shape, dtype=values.dtype, pin_memory=True)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        nbytes = C.c_size_t(0)
+
+        def call(temp_ptr):
+            return lib.cusort_sort_pairs_host(temp_ptr, C.byref(nbytes), kid, C.c_void_p(keys.data_ptr()),
+                                              C.c_void_p(out_keys.data_ptr()), vb, C.c_void_p(values.data_ptr()),
+                                              C.c_void_p(out_values.data_ptr()), n, begin_bit, end_bit,
+                                              int(descending), C.c_void_p(stream.cuda_stream))
+
+        _capi.check(call(None), "cusort_sort_pairs_host size query")
+        temp = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=dev)
+        _capi.check(call(C.c_void_p(temp.data_ptr())), "cusort_sort_pairs_host")
+        stream.synchronize()
+    return out_keys, out_values
+
+
 def _check_offsets(keys: torch.Tensor, begin_offsets: torch.Tensor, end_offsets: torch.Tensor) -> int:
     """Segment offsets: int64, 1-D, contiguous, equal lengths, on the keys' device.  Returns the
     segment count.  No CUDA call."""

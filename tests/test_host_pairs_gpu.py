@@ -77,3 +77,17 @@ def test_host_pairs_bit_range_and_empty():
     e = np.empty(0, dtype=np.uint32)
     ko, vo = run_host("u32", e, e.copy())
     assert ko.size == 0 and vo.size == 0
+
+
+def test_radix_sort_host_torch_wrapper():
+    from libcusort_b200.torch_sort import radix_sort_host
+    g = torch.Generator().manual_seed(63)
+    n = 2_000_003
+    keys = torch.randint(-(2 ** 31), 2 ** 31, (n,), dtype=torch.int64, generator=g).to(torch.int32).pin_memory()
+    vals = torch.arange(n, dtype=torch.int32).pin_memory()
+    ko, vo = radix_sort_host(keys, vals)
+    ref = torch.sort(keys, stable=True)
+    assert torch.equal(ko, ref.values) and torch.equal(vo.long(), ref.indices)
+    ko, vo = radix_sort_host(keys, vals, descending=True)
+    ref = torch.sort(keys, stable=True, descending=True)
+    assert torch.equal(ko, ref.values) and torch.equal(vo.long(), ref.indices)

@@ -109,3 +109,11 @@ def test_any_width_payloads_only_where_allowed():
     assert _check_args(k, v, None, None, None, any_width=True) == 24
     with pytest.raises(ValueError, match="24 bytes"):
         _check_args(k, v, None, None, None)
+
+
+def test_host_sort_rejects_cuda_and_bad_widths():
+    from libcusort_b200.torch_sort import radix_sort_host
+    with pytest.raises(ValueError, match="CPU"):
+        radix_sort_host(_k(10), torch.empty(10, dtype=torch.int32, device=M))
+    with pytest.raises(ValueError):
+        radix_sort_host(torch.arange(10, dtype=torch.int32), torch.empty(10, 3, dtype=torch.int8))
