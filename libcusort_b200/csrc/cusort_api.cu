@@ -761,6 +761,45 @@ cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int kt, size
 
 using namespace cusort_b200;
 
+namespace cusort_b200 {
+cudaError_t sort_pairs_direct(void* t, size_t* tb, int kt, const void* ki, void* ko, size_t vb, const void* vi,
+                              void* vo, int64_t n, int b, int e, bool desc, cudaStream_t s) {
+  SortCall c = {};
+  c.d_temp = t;
+  c.temp_bytes = tb;
+  c.kt = (int)kt;
+  c.vb = vb;
+  c.desc = desc;
+  c.raw = true;
+  c.k_in = ki;
+  c.k_out = ko;
+  c.v_in = vi;
+  c.v_out = vo;
+  c.n = n;
+  c.begin = b;
+  c.end = e;
+  c.stream = s;
+  return sort_impl(c);
+}
+}  // namespace cusort_b200
+
+// In/out-pointer SortPairs of 8-byte keys with 16-byte values over 6 or more
+// digit passes moves the keys with their 32-bit input positions through the
+// passes and gathers the values once at the end (CUSORT_INDEX_PATH=1, the
+// default): 12 instead of 24 bytes per item and pass, against one random
+// 16-byte gather.  The result is the same: both are the stable sort.
+// Measured on B200 at 2^26 (ms, direct -> index path): f64 keys + 16-byte
+// values 7.03 -> 6.20; and not taken where it lost: u64 + 8-byte values 4.84
+// -> 5.59, u32 + 16 bytes 2.92 -> 3.43, u16 + 16 bytes 1.46 -> 2.60 (random
+// 8- and 16-byte reads of the gather run far below the streaming rate).
+#ifndef CUSORT_INDEX_PATH
+#define CUSORT_INDEX_PATH 1
+#endif
+static bool index_path_pays(int kt, size_t vb, int64_t n, int b, int e) {
+  if (!CUSORT_INDEX_PATH || n < (int64_t)(1 << 20) || (uint64_t)n > 0xFFFFFFFFull || b < 0 || e <= b) return false;
+  return vb == 16 && key_bytes_of(kt) == 8 && (e - b + 7) / 8 >= 6;
+}
+
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
@@ -834,12 +873,16 @@ cudaError_t cusort_sort_keys_descending(void* t, size_t* tb, cusort_key_type kt,
 cudaError_t cusort_sort_pairs(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko, size_t vb,
                               const void* vi, void* vo, int64_t n, int b, int e, cudaStream_t s) {
   if (vb == 0) return cudaErrorInvalidValue;
+  if (index_path_pays((int)kt, vb, n, b, e))
+    return sort_pairs_by_index(t, tb, (int)kt, ki, ko, vb, vi, vo, n, b, e, 0, s);
   return sort_raw(t, tb, kt, ki, ko, vb, vi, vo, n, b, e, false, s);
 }
 cudaError_t cusort_sort_pairs_descending(void* t, size_t* tb, cusort_key_type kt, const void* ki, void* ko,
                                          size_t vb, const void* vi, void* vo, int64_t n, int b, int e,
                                          cudaStream_t s) {
   if (vb == 0) return cudaErrorInvalidValue;
+  if (index_path_pays((int)kt, vb, n, b, e))
+    return sort_pairs_by_index(t, tb, (int)kt, ki, ko, vb, vi, vo, n, b, e, 1, s);
   return sort_raw(t, tb, kt, ki, ko, vb, vi, vo, n, b, e, true, s);
 }
 

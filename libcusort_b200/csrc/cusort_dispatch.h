@@ -63,6 +63,17 @@ cudaError_t sort_db_in_scratch(void* scratch, size_t scratch_bytes, int key_type
                                struct cusort_double_buffer* keys, struct cusort_double_buffer* values,
                                int64_t num_items, int begin_bit, int end_bit, cudaStream_t stream);
 
+// In/out-pointer SortPairs without the index-path choice below
+// (cusort_api.cu).
+cudaError_t sort_pairs_direct(void* d_temp, size_t* temp_bytes, int key_type, const void* keys_in,
+                              void* keys_out, size_t value_bytes, const void* values_in, void* values_out,
+                              int64_t num_items, int begin_bit, int end_bit, bool descending, cudaStream_t stream);
+// SortPairs as the keys with their input positions, then the values gathered
+// through the sorted positions (cusort_wide.cu): any value width.
+cudaError_t sort_pairs_by_index(void* d_temp, size_t* temp_bytes, int key_type, const void* keys_in,
+                                void* keys_out, size_t value_bytes, const void* values_in, void* values_out,
+                                int64_t num_items, int begin_bit, int end_bit, int descending, cudaStream_t stream);
+
 // CUSORT_WIDE_OFFSETS=1 in the environment: sorts of any size use the 64-bit
 // offset kernels (cusort_api.cu; a test hook).
 bool force_wide_offsets();

@@ -331,3 +331,19 @@ def test_sorted_tiles(kt, vb, shift):
     vals = D.values_for(n, vb) if vb else None
     check(kt, keys, vals)
     check(kt, keys, vals, desc=True)
+
+
+@pytest.mark.parametrize("kt,vb", [("f64", 16), ("u64", 16), ("i64", 16), ("u32", 16), ("u64", 8)])
+@pytest.mark.parametrize("desc", [False, True])
+def test_index_path_for_wide_values(kt, vb, desc):
+    # from 2^20 items the in/out form sorts 8-byte keys with 16-byte values over 6+ digit passes as
+    # keys + 32-bit input positions, then gathers the values: the same stable result (the other
+    # shapes and the narrow bit range below take the direct path)
+    n = (1 << 20) + 4099
+    keys = D.special_floats(kt, n, seed=71) if kt.startswith("f") else D.uniform_bits(kt, n, seed=71)
+    keys[: n // 3] = keys[5]  # a run of equal keys keeps its input order
+    vals = D.values_for(n, vb)
+    check(kt, keys, vals, desc=desc)
+    bits = 8 * keys.dtype.itemsize
+    check(kt, keys, vals, 2, bits - 3, desc=desc)
+    check(kt, keys, vals, 0, 24, desc=desc)
