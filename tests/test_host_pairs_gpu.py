@@ -26,19 +26,19 @@ if not torch.cuda.is_available():
 CORES = os.cpu_count() or 1
 
 
-def _pinned(a: np.ndarray):
-    t = torch.empty(max(a.nbytes, 1), dtype=torch.uint8, pin_memory=True)
+def _pinned(a: np.ndarray, pin: bool = True):
+    t = torch.empty(max(a.nbytes, 1), dtype=torch.uint8, pin_memory=pin)
     if a.nbytes:
         t[: a.nbytes].copy_(torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1)))
     return t
 
 
-def run_host(kt, keys, vals, begin=0, end=None, desc=False):
+def run_host(kt, keys, vals, begin=0, end=None, desc=False, pin=True):
     lib = _capi.load()
     n = len(keys)
     end = 8 * keys.dtype.itemsize if end is None else end
     vb = vals.dtype.itemsize * int(np.prod(vals.shape[1:], dtype=np.int64))
-    kin, vin = _pinned(keys), _pinned(vals)
+    kin, vin = _pinned(keys, pin), _pinned(vals, pin)
     kout = torch.empty_like(kin)
     vout = torch.empty_like(vin)
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -64,6 +64,16 @@ def test_host_pairs_match_oracle(kt, vb, desc):
     vals = D.values_for(n, vb)
     ko, vo = run_host(kt, keys, vals, desc=desc)
     ek, ev = O.oracle_sort(kt, keys, vals, 0, None, desc, threads=CORES)
+    assert same_bits(ko, ek) and same_bits(vo, ev)
+
+
+def test_host_pairs_pageable_memory():
+    # pageable host buffers work too (the copies then do not overlap)
+    n = 500_009
+    keys = D.uniform_bits("i32", n, seed=64)
+    vals = D.values_for(n, 8)
+    ko, vo = run_host("i32", keys, vals, pin=False)
+    ek, ev = O.oracle_sort("i32", keys, vals, 0, None, False, threads=CORES)
     assert same_bits(ko, ek) and same_bits(vo, ev)
 
 
