@@ -268,6 +268,14 @@ inline void fill_segmented(SegKernels* k) {
   k->tiny.threads = 256;
   k->tiny.tile = 32;
   k->tiny.smem = 0;
+  k->small_2warps.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 2, KPT>);
+  k->small_2warps.threads = 256;
+  k->small_2warps.tile = SegSmallLayout<KB, VB, FK, 2, KPT>::CAP;
+  k->small_2warps.smem = SegSmallLayout<KB, VB, FK, 2, KPT>::SMEM;
+  k->small_4warps.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 4, KPT>);
+  k->small_4warps.threads = 256;
+  k->small_4warps.tile = SegSmallLayout<KB, VB, FK, 4, KPT>::CAP;
+  k->small_4warps.smem = SegSmallLayout<KB, VB, FK, 4, KPT>::SMEM;
   k->small_block.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 8, KPT>);
   k->small_block.threads = 256;
   k->small_block.tile = SegSmallLayout<KB, VB, FK, 8, KPT>::CAP;

@@ -239,9 +239,25 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
     e = launch(k.small_warp.func, (int)std::min<int64_t>(want, (int64_t)sms * occ), 256, k.small_warp.smem, false,
                &sa, stream);
     if (e) return e;
+    // groups of 2 and 4 warps (four and two per CTA) for the middle lengths
+    const KernelInfo* mids[2] = {&k.small_2warps, &k.small_4warps};
+    uint64_t lo = (uint64_t)k.small_warp.tile + 1;
+    for (int m = 0; m < 2; ++m) {
+      const KernelInfo& ki = *mids[m];
+      e = occupancy_of(ki, &sms, &occ);
+      if (e) return e;
+      sa.min_len = lo;
+      sa.max_len = (uint64_t)ki.tile;
+      const int64_t groups_per_cta = 4 >> m;
+      e = launch(ki.func, (int)std::min<int64_t>((num_segments + groups_per_cta - 1) / groups_per_cta,
+                                                 (int64_t)sms * occ),
+                 256, ki.smem, false, &sa, stream);
+      if (e) return e;
+      lo = (uint64_t)ki.tile + 1;
+    }
     e = occupancy_of(k.small_block, &sms, &occ);
     if (e) return e;
-    sa.min_len = (uint64_t)k.small_warp.tile + 1;
+    sa.min_len = lo;
     sa.max_len = small_cap;
     e = launch(k.small_block.func, (int)std::min<int64_t>(num_segments, (int64_t)sms * occ), 256,
                k.small_block.smem, false, &sa, stream);

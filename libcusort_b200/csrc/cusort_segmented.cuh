@@ -9,8 +9,9 @@
 //     the whole masked key by all-pairs comparison (seg_tiny_kernel);
 //   * up to 32*KPT items: one warp per segment, every pass in shared memory
 //     (seg_small_kernel<..., WPS = 1>);
-//   * up to 256*KPT items: one 256-thread CTA per segment, same scheme
-//     (seg_small_kernel<..., WPS = 8>);
+//   * up to 64*KPT, 128*KPT, 256*KPT items: groups of 2, 4 or 8 warps per
+//     segment (four, two or one per CTA), same scheme
+//     (seg_small_kernel<..., WPS = 2, 4, 8>);
 //   * longer: cut into onesweep tiles that never straddle a segment.  The
 //     planner (seg_plan_kernel) gives each such segment a slot and a run of
 //     tile numbers, seg_hist_kernel counts every pass's digits per segment,
@@ -73,9 +74,16 @@ __global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a)
   uint32_t* cnt = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS);  // [WPS][256]
   uint32_t* scan = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS + L::CNT);
   uint32_t* qual = reinterpret_cast<uint32_t*>(gb + L::KEYS + L::VALS + L::CNT + L::SCAN);
+  // the group's barrier: its warp, the CTA, or (2 or 4 warps) named barrier
+  // 1 + g, so the groups of a CTA advance independently
   auto gsync = [&]() {
-    if constexpr (WPS == 1) __syncwarp();
-    else __syncthreads();
+    if constexpr (WPS == 1) {
+      __syncwarp();
+    } else if constexpr (WPS == 8) {
+      __syncthreads();
+    } else {
+      asm volatile("bar.sync %0, %1;" ::"r"(1u + g), "r"((uint32_t)GT) : "memory");
+    }
   };
   const K* keys_in = static_cast<const K*>(a.keys_in);
   K* keys_out = static_cast<K*>(a.keys_out);
@@ -145,6 +153,34 @@ __global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a)
           cnt[w * kRadix + d] = start;
           start += c;
         }
+      } else if constexpr (WPS > 1) {
+        // 64 or 128 threads, DPT consecutive digits each
+        constexpr int DPT = kRadix / GT;
+        const uint32_t d0 = gtid * DPT;
+        uint32_t tot[DPT], sum = 0;
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) {
+          tot[j] = 0;
+#pragma unroll
+          for (int w = 0; w < WPS; ++w) tot[j] += cnt[w * kRadix + d0 + j];
+          sum += tot[j];
+        }
+        const uint32_t incl = dev::warp_inclusive_scan(sum, lane);
+        if (lane == 31) scan[wg] = incl;
+        gsync();
+        uint32_t start = incl - sum;
+        for (uint32_t w = 0; w < wg; ++w) start += scan[w];
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) {
+          uint32_t run = start;
+#pragma unroll
+          for (int w = 0; w < WPS; ++w) {
+            const uint32_t c = cnt[w * kRadix + d0 + j];
+            cnt[w * kRadix + d0 + j] = run;
+            run += c;
+          }
+          start += tot[j];
+        }
       } else {
         // one warp: lane handles digits 8*lane .. 8*lane+7
         uint32_t c[8], sum = 0;
@@ -197,10 +233,10 @@ __global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a)
       for (uint32_t m = qm; m; m &= m - 1) sort_segment(seg_at(base, (uint32_t)(__ffs(m) - 1)));
     } else {
       if (lane == 0) qual[wg] = qm;
-      __syncthreads();
+      gsync();
       for (int w = 0; w < WPS; ++w)
         for (uint32_t m = qual[w]; m; m &= m - 1) sort_segment(seg_at(base, (uint32_t)w * 32 + (uint32_t)(__ffs(m) - 1)));
-      __syncthreads();  // every thread has read qual[] before it is rewritten
+      gsync();  // every thread of the group has read qual[] before it is rewritten
     }
   }
 }
