@@ -264,10 +264,14 @@ inline void fill_segmented(SegKernels* k) {
   k->small_warp.threads = 256;
   k->small_warp.tile = SegSmallLayout<KB, VB, FK, 1, KPT>::CAP;
   k->small_warp.smem = SegSmallLayout<KB, VB, FK, 1, KPT>::SMEM;
-  k->tiny.func = reinterpret_cast<const void*>(&seg_tiny_kernel<KB, VB, FK>);
-  k->tiny.threads = 256;
-  k->tiny.tile = 32;
-  k->tiny.smem = 0;
+  static_assert(kTinyClasses == 2 && sizeof(k->tiny) / sizeof(k->tiny[0]) == kTinyClasses, "tiny classes");
+  k->tiny[0].func = reinterpret_cast<const void*>(&seg_tiny_kernel<KB, VB, FK, kTinySlotsOf[0]>);
+  k->tiny[1].func = reinterpret_cast<const void*>(&seg_tiny_kernel<KB, VB, FK, kTinySlotsOf[1]>);
+  for (int t = 0; t < kTinyClasses; ++t) {
+    k->tiny[t].threads = 256;
+    k->tiny[t].tile = 32 * kTinySlotsOf[t];
+    k->tiny[t].smem = 0;
+  }
   k->small_2warps.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 2, KPT>);
   k->small_2warps.threads = 256;
   k->small_2warps.tile = SegSmallLayout<KB, VB, FK, 2, KPT>::CAP;

@@ -207,9 +207,9 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
     return launch(get_seg_copy_kernel((int)vb), seg_grid, 256, 0, false, &c, stream);
   }
 
-  // 1. small segments: one warp per segment up to 32 items (all-pairs rank)
-  //    and up to the warp capacity (passes in shared memory), one CTA per
-  //    segment up to the block capacity
+  // 1. small segments: one warp per segment up to 128 items (all-pairs rank)
+  //    and up to the warp capacity (passes in shared memory), groups of 2 and
+  //    4 warps, then one CTA per segment up to the block capacity
   SegSmallArgs sa = {};
   sa.keys_in = kin;
   sa.keys_out = kout;
@@ -224,16 +224,23 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
   sa.passes = P;
   sa.last_mask = last_mask;
   {
-    cudaError_t e = occupancy_of(k.tiny, &sms, &occ);
-    if (e) return e;
-    sa.min_len = 1;
-    sa.max_len = (uint64_t)k.tiny.tile;
-    e = launch(k.tiny.func, (int)std::min<int64_t>((num_segments + 7) / 8, (int64_t)sms * occ), 256, 0, false, &sa,
-               stream);
-    if (e) return e;
+    // all-pairs classes: 1-32 and 33-128 items
+    cudaError_t e = cudaSuccess;
+    uint64_t lo = 1;
+    for (const KernelInfo& ki : k.tiny) {
+      e = occupancy_of(ki, &sms, &occ);
+      if (e) return e;
+      sa.min_len = lo;
+      sa.max_len = (uint64_t)ki.tile;
+      // 8 warps per CTA, 32 segments per warp and round
+      e = launch(ki.func, (int)std::min<int64_t>((num_segments + 255) / 256, (int64_t)sms * occ), 256, 0, false, &sa,
+                 stream);
+      if (e) return e;
+      lo = (uint64_t)ki.tile + 1;
+    }
     e = occupancy_of(k.small_warp, &sms, &occ);
     if (e) return e;
-    sa.min_len = (uint64_t)k.tiny.tile + 1;
+    sa.min_len = lo;
     sa.max_len = (uint64_t)k.small_warp.tile;
     const int64_t want = (num_segments + 7) / 8;
     e = launch(k.small_warp.func, (int)std::min<int64_t>(want, (int64_t)sms * occ), 256, k.small_warp.smem, false,
@@ -241,7 +248,7 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
     if (e) return e;
     // groups of 2 and 4 warps (four and two per CTA) for the middle lengths
     const KernelInfo* mids[2] = {&k.small_2warps, &k.small_4warps};
-    uint64_t lo = (uint64_t)k.small_warp.tile + 1;
+    lo = std::max<uint64_t>(lo, (uint64_t)k.small_warp.tile + 1);
     for (int m = 0; m < 2; ++m) {
       const KernelInfo& ki = *mids[m];
       e = occupancy_of(ki, &sms, &occ);

@@ -5,8 +5,9 @@
 // DeviceSegmentedRadixSort (begin/end offset arrays in device memory).
 //
 // Segments are handled by length class, with no host synchronisation:
-//   * up to 32 items: one warp per segment, one item per lane, stable rank of
-//     the whole masked key by all-pairs comparison (seg_tiny_kernel);
+//   * up to 128 items: one warp per segment, one item per lane (up to 32
+//     items) or four, stable rank of the whole masked key by all-pairs
+//     comparison (seg_tiny_kernel);
 //   * up to 32*KPT items: one warp per segment, every pass in shared memory
 //     (seg_small_kernel<..., WPS = 1>);
 //   * up to 64*KPT, 128*KPT, 256*KPT items: groups of 2, 4 or 8 warps per
@@ -57,8 +58,14 @@ struct SegSmallLayout {
   static constexpr size_t SMEM = GROUP * GROUPS;
 };
 
+// Resident CTAs per SM the small-segment kernels are compiled for (4: at most
+// 64 registers per thread).
+#ifndef CUSORT_SEG_SMALL_MIN_CTAS
+#define CUSORT_SEG_SMALL_MIN_CTAS 4
+#endif
+
 template <int KB, int VB, bool FK, int WPS, int KPT>
-__global__ void __launch_bounds__(256, 4) seg_small_kernel(const SegSmallArgs a) {
+__global__ void __launch_bounds__(256, CUSORT_SEG_SMALL_MIN_CTAS) seg_small_kernel(const SegSmallArgs a) {
   using K = typename dev::UIntOf<KB>::T;
   using V = typename dev::UIntOf<(VB ? VB : 1)>::T;
   using L = SegSmallLayout<KB, VB, FK, WPS, KPT>;
@@ -359,17 +366,66 @@ __global__ void __launch_bounds__(256) seg_scan_kernel(const SegHistArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// tiny segments (at most 32 items): one warp per segment, one item per lane,
-// every pass at once: an item's output position is the number of items whose
-// masked key (all bits of [begin_bit, end_bit), twiddled) is smaller, or equal
-// and earlier in the segment -- a stable rank by all-pairs comparison over
-// warp shuffles, then one store per item.
+// tiny segments (at most 32 * S items): one warp per segment, up to S items
+// per lane (item sl * 32 + lane in slot sl), every pass at once: an item's
+// output position is the number of items whose masked key (all bits of
+// [begin_bit, end_bit), twiddled) is smaller, or equal and earlier in the
+// segment -- a stable rank by all-pairs comparison over warp shuffles, then
+// one store per item.  Work is (length / 32) x length shuffle-compares,
+// whatever the number of passes: up to 128 items that is less than the
+// per-pass digit counts and scans of the warp class (at 200-256 items it was
+// more).  Two instances: S = 1 for 1-32 items and S = 4 for 33-128; the
+// one-slot kernel keeps four segments' loads in flight per warp.
 // ---------------------------------------------------------------------------
-template <int KB, int VB, bool FK>
+constexpr int kTinyClasses = 2;
+constexpr int kTinySlotsOf[kTinyClasses] = {1, 4};
+
+// Ranks of the U occupied slots: every valid item (slot ss, lane l) of the
+// segment is broadcast once and compared with each own item.
+template <int U, int S, typename M>
+__device__ __forceinline__ void tiny_rank(const M (&mk)[S], uint32_t (&rank)[S], uint32_t n, uint32_t lane) {
+#pragma unroll
+  for (int ss = 0; ss < U; ++ss) {
+    const uint32_t cnt = min(32u, n - (uint32_t)ss * 32u);
+#pragma unroll 4
+    for (uint32_t l = 0; l < cnt; ++l) {
+      const M o = __shfl_sync(0xffffffffu, mk[ss], l);
+#pragma unroll
+      for (int si = 0; si < U; ++si) {
+        // item (ss, l) precedes item (si, lane) in the segment when ss < si,
+        // or ss == si and l < lane
+        bool lt;
+        if (ss < si) lt = o <= mk[si];
+        else if (ss > si) lt = o < mk[si];
+        else lt = o < mk[si] || (o == mk[si] && l < lane);
+        rank[si] += lt ? 1u : 0u;
+      }
+    }
+  }
+}
+
+// tiny_rank<used> for the warp-uniform number of occupied slots
+template <int U, int S, typename M>
+__device__ __forceinline__ void tiny_rank_used(uint32_t used, const M (&mk)[S], uint32_t (&rank)[S], uint32_t n,
+                                               uint32_t lane) {
+  if constexpr (U < S) {
+    if (used <= (uint32_t)U) {
+      tiny_rank<U, S>(mk, rank, n, lane);
+      return;
+    }
+    tiny_rank_used<U + 1, S>(used, mk, rank, n, lane);
+  } else {
+    tiny_rank<S, S>(mk, rank, n, lane);
+  }
+}
+
+template <int KB, int VB, bool FK, int S>
 __global__ void __launch_bounds__(256) seg_tiny_kernel(const SegSmallArgs a) {
   using K = typename dev::UIntOf<KB>::T;
   using V = typename dev::UIntOf<(VB ? VB : 1)>::T;
   constexpr bool HAS_V = VB > 0;
+  // the masked key, compared as 32 bits when the key fits (one shuffle)
+  using M = typename std::conditional<(KB <= 4), uint32_t, unsigned long long>::type;
   const uint32_t lane = threadIdx.x & 31u;
   const K* keys_in = static_cast<const K*>(a.keys_in);
   K* keys_out = static_cast<K*>(a.keys_out);
@@ -378,42 +434,71 @@ __global__ void __launch_bounds__(256) seg_tiny_kernel(const SegSmallArgs a) {
   const K tc = (K)a.tw_c, tf = (K)a.tw_f;
   const uint32_t nbits = 8u * (a.passes - 1u) + (uint32_t)__popc(a.last_mask);
   const unsigned long long range = nbits >= 64 ? ~0ull : ((1ull << nbits) - 1ull);
-  const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
-  // the next segment's offsets are loaded while this one is sorted (one
-  // dependent round trip per segment instead of two)
-  uint64_t s = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  int64_t nb = 0, ne = 0;
-  if (s < a.num_segments) {
-    nb = a.begin_offsets[s];
-    ne = a.end_offsets[s];
-  }
-  for (; s < a.num_segments; s += warps) {
-    const int64_t b = nb, e = ne;
-    if (s + warps < a.num_segments) {
-      nb = a.begin_offsets[s + warps];
-      ne = a.end_offsets[s + warps];
+  // Warp W examines segments W*32 .. W*32+31 (one per lane, coalesced), then
+  // the next chunk NW*32 further on, and sorts the ones of its class P at a
+  // time: the P segments' loads are in flight together, and skipping the
+  // segments of other classes costs one round trip per 32 of them.
+  constexpr int P = S == 1 ? 4 : (S <= 4 ? 2 : 1);
+  const uint64_t nw = (uint64_t)gridDim.x * (blockDim.x >> 5);
+  for (uint64_t base = ((uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32u; base < a.num_segments;
+       base += nw * 32u) {
+    int64_t mb = 0, me = 0;
+    if (base + lane < a.num_segments) {
+      mb = a.begin_offsets[base + lane];
+      me = a.end_offsets[base + lane];
     }
-    const uint64_t len = e > b ? (uint64_t)(e - b) : 0;
-    if (len < a.min_len || len > a.max_len || len == 0) continue;  // uniform within the warp
-    const uint32_t n = (uint32_t)len;
-    const bool in = lane < n;
-    K k = K(0);
-    V v{};
-    if (in) {
-      k = keys_in[b + lane];
-      if constexpr (HAS_V) v = vals_in[b + lane];
-    }
-    // the masked key, compared as 32 bits when the key fits (one shuffle)
-    using M = typename std::conditional<(KB <= 4), uint32_t, unsigned long long>::type;
-    const M mk = (M)(((unsigned long long)dev::twiddle_k<FK, K>(k, tc, tf) >> a.begin_bit) & range);
-    uint32_t rank = 0;
-    for (uint32_t j = 0; j < n; ++j) {
-      const M o = __shfl_sync(0xffffffffu, mk, j);
-      rank += (o < mk || (o == mk && j < lane)) ? 1u : 0u;
-    }
-    if (in) {
-      keys_out[b + rank] = k;
-      if constexpr (HAS_V) vals_out[b + rank] = v;
+    const uint64_t len = me > mb ? (uint64_t)(me - mb) : 0;
+    uint32_t m = __ballot_sync(0xffffffffu, len != 0 && len >= a.min_len && len <= a.max_len &&
+                                                len <= (uint64_t)(32 * S));
+    while (m) {  // warp-uniform
+      int64_t sb[P];
+      uint32_t sn[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        sb[p] = 0;
+        sn[p] = 0;
+        if (m) {
+          const int j = __ffs(m) - 1;
+          m &= m - 1;
+          sb[p] = __shfl_sync(0xffffffffu, mb, j);
+          sn[p] = (uint32_t)(__shfl_sync(0xffffffffu, me, j) - sb[p]);
+        }
+      }
+      K k[P][S];
+      V v[P][HAS_V ? S : 1];
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+#pragma unroll
+        for (int sl = 0; sl < S; ++sl) {
+          const uint32_t i = (uint32_t)sl * 32u + lane;
+          k[p][sl] = K(0);
+          if constexpr (HAS_V) v[p][sl] = V{};
+          if (i < sn[p]) {
+            k[p][sl] = keys_in[sb[p] + i];
+            if constexpr (HAS_V) v[p][sl] = vals_in[sb[p] + i];
+          }
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const uint32_t n = sn[p];
+        if (n == 0) continue;  // warp-uniform
+        M mk[S];
+        uint32_t rank[S];
+#pragma unroll
+        for (int sl = 0; sl < S; ++sl) {
+          mk[sl] = (M)(((unsigned long long)dev::twiddle_k<FK, K>(k[p][sl], tc, tf) >> a.begin_bit) & range);
+          rank[sl] = 0;
+        }
+        tiny_rank_used<1, S>((n + 31u) / 32u, mk, rank, n, lane);
+#pragma unroll
+        for (int sl = 0; sl < S; ++sl) {
+          if ((uint32_t)sl * 32u + lane < n) {
+            keys_out[sb[p] + rank[sl]] = k[p][sl];
+            if constexpr (HAS_V) vals_out[sb[p] + rank[sl]] = v[p][sl];
+          }
+        }
+      }
     }
   }
 }
