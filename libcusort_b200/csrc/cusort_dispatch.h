@@ -45,6 +45,7 @@ bool get_routed_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* o
 // Segmented-sort kernels (kernels_seg_*.cu; cusort_segmented.cuh).
 struct SegKernels {
   KernelInfo onesweep, hist, scan, small_warp, small_2warps, small_4warps, small_block;
+  KernelInfo small_block2;  // one CTA per segment, twice small_block's items per thread
   KernelInfo tiny[2];  // all-pairs rank, 1 and 4 items per lane (capacity in .tile)
 };
 bool get_segmented_k12(int key_bytes, int value_bytes, int off_bytes, bool float_key, SegKernels* k);

@@ -284,6 +284,10 @@ inline void fill_segmented(SegKernels* k) {
   k->small_block.threads = 256;
   k->small_block.tile = SegSmallLayout<KB, VB, FK, 8, KPT>::CAP;
   k->small_block.smem = SegSmallLayout<KB, VB, FK, 8, KPT>::SMEM;
+  k->small_block2.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 8, 2 * KPT>);
+  k->small_block2.threads = 256;
+  k->small_block2.tile = SegSmallLayout<KB, VB, FK, 8, 2 * KPT>::CAP;
+  k->small_block2.smem = SegSmallLayout<KB, VB, FK, 8, 2 * KPT>::SMEM;
 }
 
 template <int KB, typename Off, bool FK>

@@ -147,7 +147,7 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
 
   // temp layout (see the file comment)
   const uint64_t nn = (uint64_t)n;
-  const uint64_t small_cap = (uint64_t)k.small_block.tile;
+  const uint64_t small_cap = (uint64_t)k.small_block2.tile;  // longer segments are tiled
   SegLayout L;
   L.max_slots = nn / (small_cap + 1) + 1;
   L.max_tiles = nn / (uint64_t)k.onesweep.tile + L.max_slots + 1;
@@ -265,9 +265,16 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
     e = occupancy_of(k.small_block, &sms, &occ);
     if (e) return e;
     sa.min_len = lo;
-    sa.max_len = small_cap;
+    sa.max_len = (uint64_t)k.small_block.tile;
     e = launch(k.small_block.func, (int)std::min<int64_t>(num_segments, (int64_t)sms * occ), 256,
                k.small_block.smem, false, &sa, stream);
+    if (e) return e;
+    e = occupancy_of(k.small_block2, &sms, &occ);
+    if (e) return e;
+    sa.min_len = (uint64_t)k.small_block.tile + 1;
+    sa.max_len = small_cap;
+    e = launch(k.small_block2.func, (int)std::min<int64_t>(num_segments, (int64_t)sms * occ), 256,
+               k.small_block2.smem, false, &sa, stream);
     if (e) return e;
   }
 

@@ -13,6 +13,8 @@
 //   * up to 64*KPT, 128*KPT, 256*KPT items: groups of 2, 4 or 8 warps per
 //     segment (four, two or one per CTA), same scheme
 //     (seg_small_kernel<..., WPS = 2, 4, 8>);
+//   * up to 512*KPT items: one CTA per segment with 2*KPT items per thread
+//     (seg_small_kernel<..., WPS = 8, 2*KPT>, two CTAs per SM);
 //   * longer: cut into onesweep tiles that never straddle a segment.  The
 //     planner (seg_plan_kernel) gives each such segment a slot and a run of
 //     tile numbers, seg_hist_kernel counts every pass's digits per segment,
@@ -59,13 +61,15 @@ struct SegSmallLayout {
 };
 
 // Resident CTAs per SM the small-segment kernels are compiled for (4: at most
-// 64 registers per thread).
+// 64 registers per thread).  The large CTA class (twice the items per thread
+// of its shape) is compiled for 2.
 #ifndef CUSORT_SEG_SMALL_MIN_CTAS
 #define CUSORT_SEG_SMALL_MIN_CTAS 4
 #endif
 
 template <int KB, int VB, bool FK, int WPS, int KPT>
-__global__ void __launch_bounds__(256, CUSORT_SEG_SMALL_MIN_CTAS) seg_small_kernel(const SegSmallArgs a) {
+__global__ void __launch_bounds__(256, (KPT > SegSmallShape<KB, VB>::KPT) ? 2 : CUSORT_SEG_SMALL_MIN_CTAS)
+    seg_small_kernel(const SegSmallArgs a) {
   using K = typename dev::UIntOf<KB>::T;
   using V = typename dev::UIntOf<(VB ? VB : 1)>::T;
   using L = SegSmallLayout<KB, VB, FK, WPS, KPT>;
