@@ -46,6 +46,7 @@ bool get_routed_k8(int value_bytes, int off_bytes, bool float_key, KernelInfo* o
 struct SegKernels {
   KernelInfo onesweep, hist, scan, small_warp, small_2warps, small_4warps, small_block;
   KernelInfo small_block2;  // one CTA per segment, twice small_block's items per thread
+  KernelInfo small_warp8;   // one warp per segment, 8 items per thread (func null where small_warp has <= 8)
   KernelInfo tiny[2];  // all-pairs rank, 1 and 4 items per lane (capacity in .tile)
 };
 bool get_segmented_k12(int key_bytes, int value_bytes, int off_bytes, bool float_key, SegKernels* k);

@@ -264,6 +264,16 @@ inline void fill_segmented(SegKernels* k) {
   k->small_warp.threads = 256;
   k->small_warp.tile = SegSmallLayout<KB, VB, FK, 1, KPT>::CAP;
   k->small_warp.smem = SegSmallLayout<KB, VB, FK, 1, KPT>::SMEM;
+  // shapes of 16 items per thread: a one-warp class of 8 first (no register
+  // spills; the shorter half of the one-warp lengths)
+  if constexpr (KPT > 8) {
+    k->small_warp8.func = reinterpret_cast<const void*>(&seg_small_kernel<KB, VB, FK, 1, 8>);
+    k->small_warp8.threads = 256;
+    k->small_warp8.tile = SegSmallLayout<KB, VB, FK, 1, 8>::CAP;
+    k->small_warp8.smem = SegSmallLayout<KB, VB, FK, 1, 8>::SMEM;
+  } else {
+    k->small_warp8 = KernelInfo{};
+  }
   static_assert(kTinyClasses == 2 && sizeof(k->tiny) / sizeof(k->tiny[0]) == kTinyClasses, "tiny classes");
   k->tiny[0].func = reinterpret_cast<const void*>(&seg_tiny_kernel<KB, VB, FK, kTinySlotsOf[0]>);
   k->tiny[1].func = reinterpret_cast<const void*>(&seg_tiny_kernel<KB, VB, FK, kTinySlotsOf[1]>);

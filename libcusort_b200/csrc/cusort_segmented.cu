@@ -238,11 +238,21 @@ cudaError_t seg_sort(void* d_temp, size_t* temp_bytes, int kt, size_t vb, bool d
       if (e) return e;
       lo = (uint64_t)ki.tile + 1;
     }
+    const int64_t want = (num_segments + 7) / 8;
+    if (k.small_warp8.func != nullptr) {  // one warp, 8 items per thread, before the 16-item shape
+      e = occupancy_of(k.small_warp8, &sms, &occ);
+      if (e) return e;
+      sa.min_len = lo;
+      sa.max_len = (uint64_t)k.small_warp8.tile;
+      e = launch(k.small_warp8.func, (int)std::min<int64_t>(want, (int64_t)sms * occ), 256, k.small_warp8.smem,
+                 false, &sa, stream);
+      if (e) return e;
+      lo = std::max<uint64_t>(lo, (uint64_t)k.small_warp8.tile + 1);
+    }
     e = occupancy_of(k.small_warp, &sms, &occ);
     if (e) return e;
     sa.min_len = lo;
     sa.max_len = (uint64_t)k.small_warp.tile;
-    const int64_t want = (num_segments + 7) / 8;
     e = launch(k.small_warp.func, (int)std::min<int64_t>(want, (int64_t)sms * occ), 256, k.small_warp.smem, false,
                &sa, stream);
     if (e) return e;
