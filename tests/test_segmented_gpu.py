@@ -144,7 +144,8 @@ def test_segmented_many_tiny_segments():
 def test_segmented_class_boundaries(kt):
     # lengths at the edges of the tiny class's item slots (32, 64, 96, 128: its capacity) and of the
     # one-warp, two-warp, four-warp, CTA and large-CTA classes (their capacities are 32, 64, 128, 256
-    # and 512 x the items per thread: 16 for items of up to 8 bytes, 8 up to 16), with many ties
+    # and 512 x the items per thread: 16 for items of up to 8 bytes, 8 up to 16; items of up to 8
+    # bytes also have a one-warp kernel of 8 items per thread, up to 256), with many ties
     lengths = [31, 32, 33, 63, 64, 65, 96, 97, 127, 128, 129, 255, 256, 257, 511, 512, 513, 1023, 1024, 1025,
                2047, 2048, 2049, 4095, 4096, 4097, 8191, 8192, 8193, 2, 1, 0] * 3
     b, e, n = lengths_segments(lengths, gap=2)
