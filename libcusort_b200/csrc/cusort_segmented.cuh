@@ -9,7 +9,8 @@
 //     items) or four, stable rank of the whole masked key by all-pairs
 //     comparison (seg_tiny_kernel);
 //   * up to 32*KPT items: one warp per segment, every pass in shared memory
-//     (seg_small_kernel<..., WPS = 1>);
+//     (seg_small_kernel<..., WPS = 1>; where KPT is 16, a kernel of 8 items
+//     per thread takes the lengths up to 256 first);
 //   * up to 64*KPT, 128*KPT, 256*KPT items: groups of 2, 4 or 8 warps per
 //     segment (four, two or one per CTA), same scheme
 //     (seg_small_kernel<..., WPS = 2, 4, 8>);
